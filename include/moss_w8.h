@@ -1,0 +1,163 @@
+/*
+ * moss_w8.h - C ABI of the B200 (sm_100a) hot path of the MOSS-Image int8 trainer.
+ *
+ * The library (moss_image_b200/libmoss_w8.so) exports exactly the functions declared
+ * here. Every pointer argument is a raw device (or, where stated, host) address; sizes
+ * are element counts; streams are CUDA runtime streams owned by the caller. The library
+ * never allocates device memory on behalf of a compute call and never synchronises the
+ * host inside one. Work is enqueued on the stream passed in.
+ *
+ * Return value: 0 (MOSS_OK) on success, otherwise one of the MOSS_ERR_* codes; the
+ * calling thread's last message is available from moss_last_error().
+ *
+ * Device-side failures (a bounded wait that ran out, non-finite weights seen by the
+ * quantiser) are reported asynchronously by OR-ing MOSS_STATUS_* bits into the optional
+ * `status` word (a device int32 the caller zeroes and reads back when convenient).
+ */
+#ifndef MOSS_W8_H_
+#define MOSS_W8_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MOSS_API __attribute__((visibility("default")))
+#else
+#define MOSS_API
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* moss_stream_t; /* == cudaStream_t */
+
+/* dtype codes */
+#define MOSS_DTYPE_F16 0
+#define MOSS_DTYPE_BF16 1
+#define MOSS_DTYPE_F32 2
+
+/* return codes */
+#define MOSS_OK 0
+#define MOSS_ERR_INVALID_ARGUMENT 1
+#define MOSS_ERR_UNSUPPORTED 2
+#define MOSS_ERR_CUDA 3
+#define MOSS_ERR_RING_FULL 4
+#define MOSS_ERR_NOT_FOUND 5
+
+/* device status bits */
+#define MOSS_STATUS_NONFINITE_WEIGHT 0x1
+#define MOSS_STATUS_TIMEOUT_LOAD 0x2
+#define MOSS_STATUS_TIMEOUT_MMA 0x4
+#define MOSS_STATUS_TIMEOUT_CONVERT 0x8
+#define MOSS_STATUS_TIMEOUT_EPILOGUE 0x10
+#define MOSS_STATUS_TIMEOUT_DRAIN 0x20
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+MOSS_API int moss_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+MOSS_API const char* moss_last_error(void);
+
+/*
+ * Per-output-channel symmetric int8 quantiser.
+ * Replaces the quantiser in FrozenInt8Linear.__init__ (training/quantization.py:87-91):
+ *   s[n] = max_k |float(w[n,k])| / 127 (IEEE f32 division); s[n] = 1 where it is 0;
+ *   q[n,k] = clamp(round_half_even(float(w[n,k]) / s[n]), -127, 127).
+ * w: device [n, k] row-major in w_dtype (F16/BF16/F32). q: device int8 [n, k]. scale: device
+ * f32 [n]. Non-finite input sets MOSS_STATUS_NONFINITE_WEIGHT in *status (if given).
+ */
+MOSS_API int moss_w8_quantize(const void* w, int w_dtype, int64_t n, int64_t k, int8_t* q, float* scale,
+                     int* status, moss_stream_t stream);
+
+/*
+ * Decoded weight out[n,k] = round_w(float(q[n,k]) * round_w(scale[n])) in out_dtype.
+ * Replaces _dequantize (training/quantization.py:23-24), used by the transient
+ * FrozenInt8Linear.weight accessor (training/quantization.py:112-114).
+ */
+MOSS_API int moss_w8_dequantize(const int8_t* q, const float* scale, int64_t n, int64_t k, int out_dtype,
+                       void* out, moss_stream_t stream);
+
+/*
+ * Weight-only int8 GEMM, forward:
+ *   y[m, n] = round_x( sum_k x[m,k] * dec(q)[n,k]  + round_x(bias[n])
+ *                      + lora_scale * sum_j lora_xa[m,j] * round_x(lora_b[n,j]) )
+ * with dec(q)[n,k] = round_x(round_w(q[n,k] * round_w(scale[n]))), f32 accumulation in TMEM.
+ * Replaces triton_int8_linear_forward (training/quant_kernels.py:294-334) and its kernel
+ * (:100-167); the optional LoRA term fuses the update of LoRALinear.forward
+ * (training/lora.py:85-86) into the same accumulator.
+ *   x       device [m, k] contiguous, x_dtype F16 or BF16 (the compute dtype)
+ *   q/scale device int8 [n, k] / f32 [n]; weight_dtype = the module dtype used for decode
+ *   bias    nullable device [n] in bias_dtype
+ *   lora_xa nullable device [m, lora_rank] in x_dtype (x @ lora_A^T, unscaled)
+ *   lora_b  device [n, lora_rank] in lora_b_dtype (required when lora_xa is given)
+ *   y       device [m, n] contiguous in y_dtype
+ */
+MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* q,
+                        const float* scale, int weight_dtype, int64_t n, const void* bias,
+                        int bias_dtype, const void* lora_xa, const void* lora_b, int lora_b_dtype,
+                        int64_t lora_rank, float lora_scale, void* y, int y_dtype, int* status,
+                        moss_stream_t stream);
+
+/*
+ * Weight-only int8 GEMM, grad-input (no weight gradient: the base is frozen):
+ *   dx[m, k] = round_g( sum_n dy[m,n] * dec(q)[n,k]
+ *                       + lora_scale * sum_j lora_dyb[m,j] * round_g(lora_a[j,k]) )
+ * stored in dx_dtype. The int8 weight is read in its [n, k] storage order; the transpose is
+ * expressed in the shared-memory operand layout, never materialised.
+ * Replaces triton_int8_linear_backward (training/quant_kernels.py:337-373) and its kernel
+ * (:170-228); the LoRA term is the input gradient of LoRALinear's adapter branch
+ * (training/lora.py:85-86).
+ *   dy       device [m, n] contiguous, dy_dtype F16 or BF16
+ *   lora_dyb nullable device [m, lora_rank] in dy_dtype (dy @ lora_B, unscaled)
+ *   lora_a   device [lora_rank, k] in lora_a_dtype (required when lora_dyb is given)
+ */
+MOSS_API int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
+                       const float* scale, int weight_dtype, int64_t k, const void* lora_dyb,
+                       const void* lora_a, int lora_a_dtype, int64_t lora_rank, float lora_scale,
+                       void* dx, int dx_dtype, int* status, moss_stream_t stream);
+
+/*
+ * Dense gather of a strided (non-overlapping) view into a contiguous buffer, and the
+ * inverse scatter. Used by the activation offload to turn the payload views of
+ * _offload_view (training/activation_offload.py:32-61) into one copy-engine transfer and
+ * to rebuild the original strides in _restore_layout (training/activation_offload.py:64-77).
+ * sizes/strides are host arrays of ndim (<= 8) entries, strides in elements.
+ */
+MOSS_API int moss_strided_gather(const void* src, int64_t elem_size, int ndim, const int64_t* sizes,
+                        const int64_t* strides, void* dst, moss_stream_t stream);
+MOSS_API int moss_strided_scatter(const void* src, int64_t elem_size, int ndim, const int64_t* sizes,
+                         const int64_t* strides, void* dst, moss_stream_t stream);
+
+/*
+ * Pinned-host offload ring (replaces the per-tensor pinned allocation and compute-stream
+ * copies of pack/unpack, training/activation_offload.py:116-147).
+ * The ring owns one or more cudaHostAlloc segments (grown on demand up to max_bytes and
+ * reused across steps) and issues D2H copies on `d2h` and H2D copies on `h2d`, both
+ * caller-owned streams, fenced against the compute stream with CUDA events.
+ */
+MOSS_API int moss_offload_ring_create(int device, size_t segment_bytes, size_t max_bytes, moss_stream_t d2h,
+                             moss_stream_t h2d, void** ring);
+MOSS_API int moss_offload_ring_destroy(void* ring);
+/* Copy nbytes of contiguous device memory at src to the ring once `compute` reaches this
+ * point. Returns a ticket. MOSS_ERR_RING_FULL when max_bytes would be exceeded. */
+MOSS_API int moss_offload_pack(void* ring, const void* src, size_t nbytes, moss_stream_t compute,
+                      int64_t* ticket);
+/* Start the H2D copy of a ticket's payload into dst (device, nbytes) on the h2d stream. */
+MOSS_API int moss_offload_prefetch(void* ring, int64_t ticket, void* dst);
+/* Make `compute` wait until the ticket's H2D copy is complete. */
+MOSS_API int moss_offload_wait(void* ring, int64_t ticket, moss_stream_t compute);
+/* Drop a ticket; when no ticket is live the ring rewinds to its start. */
+MOSS_API int moss_offload_release(void* ring, int64_t ticket);
+/* Host address of a ticket's payload (valid until release). */
+MOSS_API int moss_offload_host_ptr(void* ring, int64_t ticket, void** host);
+/* Counters: bytes packed, bytes restored, live tickets, reserved pinned bytes. */
+MOSS_API int moss_offload_stats(void* ring, uint64_t* d2h_bytes, uint64_t* h2d_bytes, int64_t* live,
+                       uint64_t* pinned_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOSS_W8_H_ */

@@ -1,0 +1,769 @@
+// Weight-only int8 GEMM for sm_100a: TMA -> shared-memory dequant -> tcgen05.mma -> TMEM.
+//
+// One kernel template covers both directions of the frozen int8 linear:
+//   forward (kDX = false): C[M, N] = X[M, K] * dec(W)[N, K]^T   (B operand K-major)
+//   grad-in (kDX = true):  C[M, K] = dY[M, N] * dec(W)[N, K]     (B operand MN-major)
+// In both cases the int8 weight is read in its [N, K] storage order; for the grad-input the
+// transpose lives only in the UMMA shared-memory descriptor (MN-major, 128B swizzle).
+//
+// Persistent, warp-specialised CTA (512 threads, one CTA per SM):
+//   warp 0      TMA producer: bf16 A tile (128 x 64) + int8 W tile per stage
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=256, K=16)
+//   warps 4-7   epilogue: tcgen05.ld of the accumulator, bias, rounding, global stores
+//   warps 8-15  converters: int8 -> f16/bf16 with the per-channel scale, written straight
+//               into the canonical SW128 operand layout the MMA reads
+// Accumulators are double-buffered in TMEM (2 x 256 f32 columns) so the epilogue of tile
+// i overlaps the main loop of tile i+1.
+//
+// Decode rounding follows training/quant_kernels.py:138-149 (and the eager
+// training/quantization.py:23-24): dec = round_v(round_w(q * round_w(s))), with v the
+// compute dtype and w the module (weight) dtype. For v == w the converter uses an exact
+// integer trick (see dequant_word_bf16/_f16); the rare v != w case decodes in f32.
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "errors.cuh"
+
+namespace moss {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kStages = 4;   // A + int8 W stages
+constexpr int kBStages = 2;  // converted 16-bit B stages
+constexpr int kConvWarps = 8;
+constexpr int kEpiWarp0 = 4;
+constexpr int kConvWarp0 = 8;
+constexpr int kThreads = 16 * 32;
+constexpr uint32_t kABytes = BM * BK * 2;  // 16 KB
+constexpr uint32_t kWBytes = BN * BK;      // 16 KB
+constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kDataBytes = kStages * (kABytes + kWBytes) + kBStages * kBBytes;
+constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 256;
+
+struct Args {
+  int M, Nc, Kr;            // C[M, Nc] = A[M, Kr] * B[Kr, Nc]
+  int tiles_m, tiles_n;
+  int main_kb, num_kb;      // k-blocks from the int8 weight, total (incl. LoRA extension)
+  int manual;               // 1: producer uses plain loads (shapes TMA cannot describe)
+  const void* a; int64_t lda;
+  const int8_t* w; int64_t ldw; int w_rows, w_cols;
+  const float* scale;
+  int w_kind;
+  const void* bias; int bias_kind;
+  void* out; int out_kind; int64_t ldo;
+  const void* ext_a; int64_t ld_ext_a;             // LoRA: [M, r] (value dtype)
+  const void* ext_b; int ext_b_kind; int64_t ld_ext_b; int ext_r;  // fwd [Nc, r]; dx [r, Nc]
+  float ext_scale;
+  int* status;
+};
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t b_full[kBStages];
+  uint64_t b_empty[kBStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Barriers) <= 256, "barrier block too large");
+
+// --------------------------------------------------------------------------------------------
+// int8 -> 16-bit decode of one 32-bit word (4 codes) into two packed pairs.
+//
+// bf16: for a code q with raw byte b, A = bf16 bits 0x4300 | (b & 0x7F) = 128 + (b & 127) and
+// C = 0x4300 | (b & 0x80) = 128 or 256. A - C = q exactly (two's complement), then one
+// round-to-nearest bf16 multiply by bf16(s) gives bf16(q * bf16(s)) exactly as the reference.
+__device__ __forceinline__ void dequant_word_bf16(uint32_t w, __nv_bfloat162 s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t t01 = prmt(w, 0x43u, 0x4140u);  // 0x43 b1 0x43 b0
+  const uint32_t t23 = prmt(w, 0x43u, 0x4342u);
+  const uint32_t a01 = t01 & 0xFF7FFF7Fu, c01 = t01 & 0xFF80FF80u;
+  const uint32_t a23 = t23 & 0xFF7FFF7Fu, c23 = t23 & 0xFF80FF80u;
+  __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a01),
+                               *reinterpret_cast<const __nv_bfloat162*>(&c01));
+  __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a23),
+                               *reinterpret_cast<const __nv_bfloat162*>(&c23));
+  x01 = __hmul2(x01, s2);
+  x23 = __hmul2(x23, s2);
+  lo = *reinterpret_cast<uint32_t*>(&x01);
+  hi = *reinterpret_cast<uint32_t*>(&x23);
+}
+
+// f16: 0x6400 | (b ^ 0x80) is the half 1024 + q + 128 exactly; subtracting 1152 gives q.
+__device__ __forceinline__ void dequant_word_f16(uint32_t w, __half2 s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t t01 = prmt(u, 0x64u, 0x4140u);
+  const uint32_t t23 = prmt(u, 0x64u, 0x4342u);
+  const __half2 magic = __half2half2(__ushort_as_half(0x6480));  // 1152
+  __half2 x01 = __hsub2(*reinterpret_cast<const __half2*>(&t01), magic);
+  __half2 x23 = __hsub2(*reinterpret_cast<const __half2*>(&t23), magic);
+  x01 = __hmul2(x01, s2);
+  x23 = __hmul2(x23, s2);
+  lo = *reinterpret_cast<uint32_t*>(&x01);
+  hi = *reinterpret_cast<uint32_t*>(&x23);
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, int v_kind) {
+  if (v_kind == kBF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Generic decode (weight dtype differs from the compute dtype): f32 arithmetic.
+__device__ __forceinline__ void dequant_word_generic(uint32_t w, float s_w, int w_kind, int v_kind,
+                                                     uint32_t& lo, uint32_t& hi) {
+  float d[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float q = static_cast<float>(static_cast<int8_t>((w >> (8 * i)) & 0xFF));
+    d[i] = round_to_kind(q * s_w, w_kind);
+  }
+  lo = pack2(d[0], d[1], v_kind);
+  hi = pack2(d[2], d[3], v_kind);
+}
+
+// Per-row decode context (scale in the right representation for each path).
+template <int kV, bool kFast>
+struct Dec {
+  uint32_t s2;   // packed pair of round_v(s) for the fast paths
+  float s_w;     // round_w(s) for the generic path
+  __device__ __forceinline__ void set(float s, int w_kind) {
+    if constexpr (kFast) {
+      if constexpr (kV == kBF16) {
+        __nv_bfloat162 h = __bfloat162bfloat162(__float2bfloat16_rn(s));
+        s2 = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __half2half2(__float2half_rn(s));
+        s2 = *reinterpret_cast<uint32_t*>(&h);
+      }
+    } else {
+      s_w = round_to_kind(s, w_kind);
+    }
+  }
+  __device__ __forceinline__ void word(uint32_t w, int w_kind, uint32_t& lo, uint32_t& hi) const {
+    if constexpr (kFast) {
+      if constexpr (kV == kBF16) {
+        dequant_word_bf16(w, *reinterpret_cast<const __nv_bfloat162*>(&s2), lo, hi);
+      } else {
+        dequant_word_f16(w, *reinterpret_cast<const __half2*>(&s2), lo, hi);
+      }
+    } else {
+      dequant_word_generic(w, s_w, w_kind, kV, lo, hi);
+    }
+  }
+  // 16 codes -> 32 bytes of 16-bit operand
+  __device__ __forceinline__ void chunk(uint4 q, int w_kind, uint4& o0, uint4& o1) const {
+    word(q.x, w_kind, o0.x, o0.y);
+    word(q.y, w_kind, o0.z, o0.w);
+    word(q.z, w_kind, o1.x, o1.y);
+    word(q.w, w_kind, o1.z, o1.w);
+  }
+};
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Byte offset of element (row, col) of a 16-bit K-major SW128 tile (rows of 64 elements).
+__device__ __forceinline__ uint32_t sw128_kmajor_off16(int row, int col) {
+  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ (row & 7)) & 7) << 4) +
+                               (col & 7) * 2);
+}
+
+// Load 16 consecutive values of a float-kind row as f32 with bounds (used for LoRA blocks).
+__device__ __forceinline__ void load16_f32(const void* base, int kind, int64_t row_off, int col0, int ncols,
+                                           float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = col0 + i;
+    v[i] = (c < ncols) ? load_as_float(base, kind, row_off + c) : 0.0f;
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+template <bool kDX, int kV, bool kFast>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_ext, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw_base);
+  const uint32_t a_smem = base;
+  const uint32_t w_smem = base + kStages * kABytes;
+  const uint32_t b_smem = w_smem + kStages * kWBytes;
+  Barriers* bars = reinterpret_cast<Barriers*>(base_ptr + kDataBytes);
+  auto bar = [&](uint64_t& b) { return smem_u32(&b); };
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(bars->full[s]), 1);
+      mbar_init(bar(bars->empty[s]), 1 + kConvWarps);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(bar(bars->b_full[s]), kConvWarps);
+      mbar_init(bar(bars->b_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(bars->acc_full[s]), 1);
+      mbar_init(bar(bars->acc_empty[s]), 4);
+    }
+    mbar_init(bar(bars->drain), 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (!args.manual && lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_w);
+      if (args.ext_r > 0) tma_prefetch_desc(&tm_ext);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used_mask = 0;        // stages that received a TMA copy
+    uint32_t last_phase_mask = 0;  // phase bit of the last copy per stage
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int m0 = (t % args.tiles_m) * BM;
+      const int n0 = (t / args.tiles_m) * BN;
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        if (!mbar_wait(bar(bars->empty[stage]), phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
+          ok = false;
+          break;
+        }
+        const bool ext = kb >= args.main_kb;
+        const uint32_t a_dst = a_smem + stage * kABytes;
+        const uint32_t w_dst = w_smem + stage * kWBytes;
+        if (!args.manual) {
+          if (lane == 0) {
+            const uint32_t fb = bar(bars->full[stage]);
+            if (!ext) {
+              mbar_arrive_expect_tx(fb, kABytes + kWBytes);
+              tma_load_2d(a_dst, &tm_a, fb, kb * BK, m0);
+              if constexpr (!kDX) {
+                tma_load_2d(w_dst, &tm_w, fb, kb * BK, n0);
+              } else {
+                tma_load_2d(w_dst, &tm_w, fb, n0, kb * BK);
+                tma_load_2d(w_dst + kWBytes / 2, &tm_w, fb, n0 + 128, kb * BK);
+              }
+            } else {
+              mbar_arrive_expect_tx(fb, kABytes);
+              tma_load_2d(a_dst, &tm_ext, fb, (kb - args.main_kb) * BK, m0);
+            }
+            used_mask |= 1u << stage;
+            last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+          }
+        } else {
+          // Plain loads into the exact layouts TMA would have produced.
+          const uint16_t* asrc = static_cast<const uint16_t*>(ext ? args.ext_a : args.a);
+          const int64_t lda = ext ? args.ld_ext_a : args.lda;
+          const int acols = ext ? args.ext_r : args.Kr;
+          const int k0 = (ext ? (kb - args.main_kb) : kb) * BK;
+          uint8_t* a_ptr = base_ptr + (a_dst - base);
+          for (int idx = lane; idx < BM * BK; idx += 32) {
+            const int r = idx / BK, c = idx % BK;
+            const int gm = m0 + r, gk = k0 + c;
+            const uint16_t v = (gm < args.M && gk < acols) ? asrc[static_cast<int64_t>(gm) * lda + gk] : 0;
+            *reinterpret_cast<uint16_t*>(a_ptr + sw128_kmajor_off16(r, c)) = v;
+          }
+          if (!ext) {
+            uint8_t* w_ptr = base_ptr + (w_dst - base);
+            if constexpr (!kDX) {
+              for (int idx = lane; idx < BN * BK; idx += 32) {
+                const int r = idx / BK, c = idx % BK;
+                const int gn = n0 + r, gk = kb * BK + c;
+                w_ptr[r * BK + c] = (gn < args.w_rows && gk < args.w_cols)
+                                        ? static_cast<uint8_t>(args.w[static_cast<int64_t>(gn) * args.ldw + gk])
+                                        : 0;
+              }
+            } else {
+              for (int idx = lane; idx < BK * BN; idx += 32) {
+                const int r = idx / BN, c = idx % BN;  // r: reduction row (n), c: output col (k)
+                const int gn = kb * BK + r, gk = n0 + c;
+                const uint8_t v = (gn < args.w_rows && gk < args.w_cols)
+                                      ? static_cast<uint8_t>(args.w[static_cast<int64_t>(gn) * args.ldw + gk])
+                                      : 0;
+                const int box = c >> 7, c8 = (c & 127) >> 4;
+                w_ptr[box * (kWBytes / 2) + r * 128 + (((c8 ^ (r & 7)) & 7) << 4) + (c & 15)] = v;
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(bars->full[stage]));
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Drain: never leave with our own TMA copies still writing into shared memory.
+    if (!args.manual && lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        if (!((used_mask >> s) & 1u)) continue;
+        const long long start = clock64();
+        while (!mbar_try_wait(bar(bars->full[s]), (last_phase_mask >> s) & 1u)) {
+          if (clock64() - start > kWaitBudgetCycles) {
+            report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = umma_idesc_f16(kV == kBF16 ? 1u : 0u, kDX, BM, BN);
+    int stage = 0, bstage = 0;
+    uint32_t phase = 0, bphase = 0;
+    int it = 0;
+    bool ok = true;
+    bool issued_any = false;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(bar(bars->acc_empty[acc]), acc_phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        if (!mbar_wait(bar(bars->full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA) ||
+            !mbar_wait(bar(bars->b_full[bstage]), bphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_base = a_smem + stage * kABytes;
+          const uint32_t b_base = b_smem + bstage * kBBytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = umma_desc_sw128(a_base + kk * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (!kDX) {
+              bdesc = umma_desc_sw128(b_base + kk * 32, 16, 1024);
+            } else {
+              bdesc = umma_desc_sw128(b_base + kk * 2048, 8192, 1024);
+            }
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(bar(bars->empty[stage]));
+          umma_commit(bar(bars->b_empty[bstage]));
+          issued_any = true;
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(bar(bars->acc_full[acc]));
+      __syncwarp();
+    }
+    // Drain: all issued MMAs must retire before TMEM is released.
+    if (lane == 0 && issued_any) {
+      umma_commit(bar(bars->drain));
+      const long long start = clock64();
+      while (!mbar_try_wait(bar(bars->drain), 0)) {
+        if (clock64() - start > kWaitBudgetCycles) {
+          report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_EPILOGUE))
+        break;
+      tc_fence_after();
+      const int m0 = (t % args.tiles_m) * BM;
+      const int n0 = (t / args.tiles_m) * BN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 7) == 0) &&
+                          ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32), r);
+        tmem_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(bars->acc_empty[acc]));
+        }
+        const int col0 = n0 + c * 32;
+        if (col0 >= args.Nc) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(r[j]);
+          if constexpr (!kDX) {
+            if (args.bias != nullptr && col0 + j < args.Nc)
+              x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+          }
+          v[j] = round_to_kind(x, kV);
+        }
+        if (!row_ok) continue;
+        const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
+        if (vec_ok && col0 + 32 <= args.Nc) {
+          uint32_t p[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + off);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, v[j]);
+        }
+      }
+    }
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters
+    const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..255
+    int stage = 0, bstage = 0;
+    uint32_t phase = 0, bphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int n0 = (t / args.tiles_m) * BN;
+      // forward: this thread always handles tile rows (ct >> 2) + 64 j, j = 0..3
+      Dec<kV, kFast> dec_f[4];
+      if constexpr (!kDX) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int gn = n0 + (ct >> 2) + 64 * j;
+          dec_f[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+        }
+      }
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        if (!mbar_wait(bar(bars->full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT) ||
+            !mbar_wait(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+          ok = false;
+          break;
+        }
+        const uint32_t w_base = w_smem + stage * kWBytes;
+        const uint32_t b_base = b_smem + bstage * kBBytes;
+        const bool ext = kb >= args.main_kb;
+        if constexpr (!kDX) {
+          const int c = ct & 3;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int row = (ct >> 2) + 64 * j;
+            uint4 o0, o1;
+            if (!ext) {
+              const uint4 qv = lds128(w_base + row * 64 + c * 16);
+              dec_f[j].chunk(qv, args.w_kind, o0, o1);
+            } else {
+              float f[16];
+              const int gn = n0 + row;
+              if (gn < args.Nc) {
+                load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gn) * args.ld_ext_b,
+                           (kb - args.main_kb) * BK + c * 16, args.ext_r, f);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+              }
+              o0 = make_uint4(pack2(f[0] * args.ext_scale, f[1] * args.ext_scale, kV),
+                              pack2(f[2] * args.ext_scale, f[3] * args.ext_scale, kV),
+                              pack2(f[4] * args.ext_scale, f[5] * args.ext_scale, kV),
+                              pack2(f[6] * args.ext_scale, f[7] * args.ext_scale, kV));
+              o1 = make_uint4(pack2(f[8] * args.ext_scale, f[9] * args.ext_scale, kV),
+                              pack2(f[10] * args.ext_scale, f[11] * args.ext_scale, kV),
+                              pack2(f[12] * args.ext_scale, f[13] * args.ext_scale, kV),
+                              pack2(f[14] * args.ext_scale, f[15] * args.ext_scale, kV));
+            }
+            const uint32_t rbase = b_base + (row >> 3) * 1024 + (row & 7) * 128;
+            sts128(rbase + ((((2 * c) ^ (row & 7)) & 7) << 4), o0);
+            sts128(rbase + ((((2 * c + 1) ^ (row & 7)) & 7) << 4), o1);
+          }
+        } else {
+          // grad-input: rows are reduction indices; this thread owns one row per stage.
+          const int cw = ct >> 5;
+          const int ph = lane >> 3;
+          const int hi = (lane >> 2) & 1;
+          const int qd = lane & 3;
+          const int r_in = hi ? (ph ^ 5) : ph;  // row pairs (0,5) (1,4) (2,7) (3,6)
+          const int row = cw * 8 + r_in;
+          Dec<kV, kFast> dec;
+          if (!ext) {
+            const int gn = kb * BK + row;
+            dec.set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+          }
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            const int c16 = 4 * a + qd;
+            uint4 o0, o1;
+            if (!ext) {
+              const int box = a >> 1, c8 = 4 * (a & 1) + qd;
+              const uint4 qv = lds128(w_base + box * (kWBytes / 2) + row * 128 + (((c8 ^ r_in) & 7) << 4));
+              dec.chunk(qv, args.w_kind, o0, o1);
+            } else {
+              float f[16];
+              const int gj = (kb - args.main_kb) * BK + row;
+              if (gj < args.ext_r) {
+                load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gj) * args.ld_ext_b, n0 + c16 * 16,
+                           args.Nc, f);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+              }
+              o0 = make_uint4(pack2(f[0] * args.ext_scale, f[1] * args.ext_scale, kV),
+                              pack2(f[2] * args.ext_scale, f[3] * args.ext_scale, kV),
+                              pack2(f[4] * args.ext_scale, f[5] * args.ext_scale, kV),
+                              pack2(f[6] * args.ext_scale, f[7] * args.ext_scale, kV));
+              o1 = make_uint4(pack2(f[8] * args.ext_scale, f[9] * args.ext_scale, kV),
+                              pack2(f[10] * args.ext_scale, f[11] * args.ext_scale, kV),
+                              pack2(f[12] * args.ext_scale, f[13] * args.ext_scale, kV),
+                              pack2(f[14] * args.ext_scale, f[15] * args.ext_scale, kV));
+            }
+            const uint32_t rbase = b_base + a * (kBBytes / 4) + row * 128;
+            sts128(rbase + ((((2 * qd) ^ r_in) & 7) << 4), o0);
+            sts128(rbase + ((((2 * qd + 1) ^ r_in) & 7) << 4), o1);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(bars->b_full[bstage]));
+          mbar_arrive(bar(bars->empty[stage]));
+        }
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// K == 0: the product is empty, y = round(bias) (or zeros).
+__global__ void fill_bias_kernel(int M, int N, const void* bias, int bias_kind, int v_kind, void* out, int out_kind,
+                                 int64_t ldo) {
+  const int64_t total = static_cast<int64_t>(M) * N;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / N, c = i % N;
+    const float b = bias ? round_to_kind(load_as_float(bias, bias_kind, c), v_kind) : 0.0f;
+    store_from_float(out, out_kind, r * ldo + c, round_to_kind(b, v_kind));
+  }
+}
+
+// --------------------------------------------------------------------------------------------
+// host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, uint64_t inner,
+                     uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (row_bytes & 15) != 0) return false;
+  if ((static_cast<uint64_t>(box_inner) * esize) % 16 != 0) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+template <bool kDX, int kV, bool kFast>
+static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& te, const Args& a,
+                        cudaStream_t stream) {
+  auto kern = w8_gemm_kernel<kDX, kV, kFast>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  MOSS_CUDA_TRY(attr_err);
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = std::min(tiles, sm_count());
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(ta, tw, te, a);
+  MOSS_CUDA_TRY(cudaGetLastError());
+  return MOSS_OK;
+}
+
+template <bool kDX>
+static int dispatch(int v_kind, bool fast, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& te,
+                    const Args& a, cudaStream_t s) {
+  if (v_kind == kBF16) {
+    return fast ? launch_typed<kDX, kBF16, true>(ta, tw, te, a, s) : launch_typed<kDX, kBF16, false>(ta, tw, te, a, s);
+  }
+  return fast ? launch_typed<kDX, kF16, true>(ta, tw, te, a, s) : launch_typed<kDX, kF16, false>(ta, tw, te, a, s);
+}
+
+// Shared driver for both directions.
+//   A: [M, Kr] in v_kind (x or dy); weight q: [w_rows, w_cols]; C: [M, Nc]
+static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, int64_t Nc, const int8_t* q,
+               const float* scale, int w_kind, int64_t w_rows, int64_t w_cols, const void* bias, int bias_kind,
+               const void* ext_a, const void* ext_b, int ext_b_kind, int64_t ext_r, float ext_scale, void* out,
+               int out_kind, int* status, cudaStream_t stream) {
+  if (M < 0 || Kr < 0 || Nc < 0) return fail(MOSS_ERR_INVALID_ARGUMENT, "negative GEMM shape");
+  if (v_kind != kBF16 && v_kind != kF16)
+    return fail(MOSS_ERR_UNSUPPORTED, "compute dtype must be float16 or bfloat16 (got code %d)", v_kind);
+  if (!is_float_kind(w_kind) || !is_float_kind(out_kind))
+    return fail(MOSS_ERR_UNSUPPORTED, "unsupported weight/output dtype code");
+  if (bias != nullptr && !is_float_kind(bias_kind)) return fail(MOSS_ERR_UNSUPPORTED, "unsupported bias dtype code");
+  if (M > INT32_MAX || Kr > INT32_MAX || Nc > INT32_MAX) return fail(MOSS_ERR_INVALID_ARGUMENT, "GEMM dimension too large");
+  if (ext_a != nullptr) {
+    if (ext_b == nullptr || ext_r <= 0 || ext_r > 256 || !is_float_kind(ext_b_kind))
+      return fail(MOSS_ERR_INVALID_ARGUMENT, "LoRA operands need rank in [1, 256] and both factors");
+  }
+  if (M == 0 || Nc == 0) return clear_ok();
+  if (out == nullptr || a_ptr == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  if (Kr == 0 && ext_a == nullptr) {
+    const int64_t total = M * Nc;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4096));
+    fill_bias_kernel<<<grid, 256, 0, stream>>>(static_cast<int>(M), static_cast<int>(Nc), dx ? nullptr : bias,
+                                               bias_kind, v_kind, out, out_kind, Nc);
+    MOSS_CUDA_TRY(cudaGetLastError());
+    return clear_ok();
+  }
+  if (q == nullptr || scale == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null weight or scale pointer");
+
+  Args a{};
+  a.M = static_cast<int>(M);
+  a.Nc = static_cast<int>(Nc);
+  a.Kr = static_cast<int>(Kr);
+  a.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  a.tiles_n = static_cast<int>((Nc + BN - 1) / BN);
+  a.main_kb = static_cast<int>((Kr + BK - 1) / BK);
+  const int ext_kb = ext_a ? static_cast<int>((ext_r + BK - 1) / BK) : 0;
+  a.num_kb = a.main_kb + ext_kb;
+  a.a = a_ptr;
+  a.lda = Kr;
+  a.w = q;
+  a.ldw = w_cols;
+  a.w_rows = static_cast<int>(w_rows);
+  a.w_cols = static_cast<int>(w_cols);
+  a.scale = scale;
+  a.w_kind = w_kind;
+  a.bias = dx ? nullptr : bias;
+  a.bias_kind = bias_kind;
+  a.out = out;
+  a.out_kind = out_kind;
+  a.ldo = Nc;
+  a.ext_a = ext_a;
+  a.ld_ext_a = ext_r;
+  a.ext_b = ext_b;
+  a.ext_b_kind = ext_b_kind;
+  a.ld_ext_b = dx ? Nc : ext_r;
+  a.ext_r = ext_a ? static_cast<int>(ext_r) : 0;
+  a.ext_scale = ext_scale;
+  a.status = status;
+
+  CUtensorMap ta, tw, te;
+  memset(&ta, 0, sizeof(ta));
+  memset(&tw, 0, sizeof(tw));
+  memset(&te, 0, sizeof(te));
+  const CUtensorMapDataType v_dt = v_kind == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  bool tma = make_map(&ta, v_dt, 2, a_ptr, Kr, M, Kr * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (tma) {
+    if (!dx)
+      tma = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, w_cols, w_rows, w_cols, BK, BN,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    else
+      tma = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, w_cols, w_rows, w_cols, 128, BK,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (tma && ext_a != nullptr)
+    tma = make_map(&te, v_dt, 2, ext_a, ext_r, M, ext_r * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  a.manual = tma ? 0 : 1;
+  const bool fast = (w_kind == v_kind);
+  return dx ? dispatch<true>(v_kind, fast, ta, tw, te, a, stream) : dispatch<false>(v_kind, fast, ta, tw, te, a, stream);
+}
+
+}  // namespace gemm
+}  // namespace moss
+
+using namespace moss;
+
+extern "C" int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* q,
+                                   const float* scale, int weight_dtype, int64_t n, const void* bias, int bias_dtype,
+                                   const void* lora_xa, const void* lora_b, int lora_b_dtype, int64_t lora_rank,
+                                   float lora_scale, void* y, int y_dtype, int* status, moss_stream_t stream) {
+  const int rc = gemm::run(false, x, x_dtype, m, k, n, q, scale, weight_dtype, n, k, bias, bias_dtype, lora_xa, lora_b,
+                           lora_b_dtype, lora_rank, lora_scale, y, y_dtype, status,
+                           reinterpret_cast<cudaStream_t>(stream));
+  return rc == MOSS_OK ? clear_ok() : rc;
+}
+
+extern "C" int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
+                                  const float* scale, int weight_dtype, int64_t k, const void* lora_dyb,
+                                  const void* lora_a, int lora_a_dtype, int64_t lora_rank, float lora_scale, void* dx,
+                                  int dx_dtype, int* status, moss_stream_t stream) {
+  const int rc = gemm::run(true, dy, dy_dtype, m, n, k, q, scale, weight_dtype, n, k, nullptr, 0, lora_dyb, lora_a,
+                           lora_a_dtype, lora_rank, lora_scale, dx, dx_dtype, status,
+                           reinterpret_cast<cudaStream_t>(stream));
+  return rc == MOSS_OK ? clear_ok() : rc;
+}

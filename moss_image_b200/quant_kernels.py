@@ -1,0 +1,305 @@
+"""Backend selection, validation and launchers for the sm_100a weight-only int8 linear.
+
+Mirrors the host interface of ``training/quant_kernels.py`` (backend strings, validation
+messages, autocast dtype rule, ``out=`` buffers) so callers of the reference switch
+without edits. Differences, by design:
+
+* every accepted backend string (``auto``, ``eager``, ``triton``) executes the B200
+  tcgen05 kernels of ``libmoss_w8.so`` on CUDA tensors; there is no Triton and no CPU
+  fallback - CPU tensors raise ``RuntimeError``;
+* the compute dtype must be float16 or bfloat16 (the tcgen05 ``kind::f16`` path); a
+  float32 compute dtype raises ``RuntimeError`` with a message saying so.
+"""
+
+from __future__ import annotations
+
+from typing import Literal
+
+import torch
+
+from . import _lib
+
+QuantizedBackend = Literal["auto", "eager", "triton"]
+
+_BACKENDS = {"auto", "eager", "triton"}
+
+_status_buffers: dict[tuple[str, int | None], torch.Tensor] = {}
+
+
+def validate_quantized_backend(backend: str) -> QuantizedBackend:
+    """Reference: training/quant_kernels.py:30-33 (same accepted strings and message)."""
+    if backend not in _BACKENDS:
+        raise ValueError("quantized backend must be auto, eager or triton.")
+    return backend  # type: ignore[return-value]
+
+
+def kernels_are_available() -> bool:
+    """Whether the CUDA library loads and a CUDA device is visible."""
+    return _lib.is_available() and torch.cuda.is_available()
+
+
+# Reference name (training/quant_kernels.py:36-38); here it reports the B200 kernels.
+triton_is_available = kernels_are_available
+
+
+def _unsupported_reason(tokens: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor) -> str | None:
+    """Reference: training/quant_kernels.py:41-61, adapted to the sm_100a kernels."""
+    if not _lib.is_available():
+        try:
+            _lib.library()
+        except RuntimeError as error:
+            return f"the CUDA library is unavailable ({error})"
+    if tokens.device.type != "cuda":
+        return "the input is not on CUDA"
+    if weight.device != tokens.device or scale.device != tokens.device:
+        return "the quantized weight and scale are not on the input CUDA device"
+    if tokens.dtype not in {torch.float16, torch.bfloat16, torch.float32}:
+        return f"input dtype {tokens.dtype} is unsupported"
+    if weight.dtype != torch.int8 or scale.dtype != torch.float32:
+        return "weights must be int8 and scales must be float32"
+    if tokens.ndim < 1 or tokens.shape[-1] != weight.shape[1]:
+        return "input and weight dimensions do not match"
+    if not weight.is_contiguous() or not scale.is_contiguous():
+        return "weight and scale must be contiguous"
+    return None
+
+
+def resolve_quantized_backend(
+    backend: str,
+    tokens: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+) -> QuantizedBackend:
+    """Validate the backend string and that the sm_100a kernels can run these tensors.
+
+    Reference: training/quant_kernels.py:64-79. Unlike the reference, ``auto`` and
+    ``eager`` do not fall back to a CPU or dequantise-then-cuBLAS path: an input the
+    kernels cannot run raises ``RuntimeError``.
+    """
+    selected = validate_quantized_backend(backend)
+    reason = _unsupported_reason(tokens, weight, scale)
+    if reason is not None:
+        raise RuntimeError(f"int8 quantized backend is unavailable: {reason}.")
+    return selected
+
+
+def autocast_compute_dtype(tokens: torch.Tensor, module_dtype: torch.dtype) -> torch.dtype:
+    """Match CUDA autocast's output dtype for a linear operation.
+
+    Reference: training/quant_kernels.py:82-95.
+    """
+    if tokens.device.type != "cuda":
+        return module_dtype
+    if not torch.is_autocast_enabled("cuda"):
+        return module_dtype
+    return torch.get_autocast_dtype("cuda")
+
+
+def status_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels OR their MOSS_STATUS_* bits into."""
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    buf = _status_buffers.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key[1]))
+        _status_buffers[key] = buf
+    return buf
+
+
+def check_device_status(device: torch.device | None = None, *, reset: bool = True) -> int:
+    """Synchronise on the status word and raise if a kernel reported a failure."""
+    devices = [device] if device is not None else [torch.device("cuda", k[1]) for k in _status_buffers]
+    worst = 0
+    for dev in devices:
+        buf = status_buffer(dev)
+        value = int(buf.item())
+        if reset and value:
+            buf.zero_()
+        worst |= value
+    if worst & _lib.STATUS_TIMEOUT_MASK:
+        raise RuntimeError(f"sm_100a int8 kernel reported a pipeline timeout (status 0x{worst:x}).")
+    return worst
+
+
+def _compute_kind(dtype: torch.dtype) -> int:
+    if dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(
+            f"int8 quantized backend is unavailable: compute dtype {dtype} is unsupported "
+            "(the sm_100a kernels compute in float16 or bfloat16; use autocast or a half-precision module)."
+        )
+    return _lib.DTYPE_CODES[dtype]
+
+
+def _matrix_view(tokens: torch.Tensor) -> torch.Tensor:
+    return tokens.reshape(-1, tokens.shape[-1])
+
+
+def int8_linear_forward(
+    tokens: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None,
+    output_dtype: torch.dtype,
+    weight_dtype: torch.dtype,
+    *,
+    out: torch.Tensor | None = None,
+    lora_xa: torch.Tensor | None = None,
+    lora_b: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
+) -> torch.Tensor:
+    """Y = X dec(W)^T (+ bias) (+ lora_scale * lora_xa lora_b^T) on the sm_100a kernel.
+
+    Reference: ``triton_int8_linear_forward``, training/quant_kernels.py:294-334 (same
+    arguments and ``out=`` contract). ``tokens`` is cast to ``output_dtype`` (as the
+    reference's kernel casts its tile loads) and made contiguous if needed.
+    """
+    v_kind = _compute_kind(output_dtype)
+    matrix = _matrix_view(tokens)
+    if matrix.dtype != output_dtype:
+        matrix = matrix.to(output_dtype)
+    if not matrix.is_contiguous():
+        matrix = matrix.contiguous()
+    rows, in_features = matrix.shape
+    out_features = weight.shape[0]
+    if out is None:
+        output = torch.empty((rows, out_features), device=tokens.device, dtype=output_dtype)
+    else:
+        output = out.reshape(rows, out_features)
+        if output.dtype != output_dtype or not output.is_contiguous():
+            raise ValueError("int8 output buffer has the wrong dtype or is not contiguous.")
+    if bias is not None and (bias.device != tokens.device or not bias.is_contiguous()):
+        raise RuntimeError("int8 quantized bias must be contiguous and on the input device.")
+    rank = 0
+    if lora_xa is not None:
+        if lora_b is None:
+            raise ValueError("lora_xa needs lora_b")
+        lora_xa = lora_xa.reshape(rows, -1)
+        if lora_xa.dtype != output_dtype or not lora_xa.is_contiguous():
+            lora_xa = lora_xa.to(output_dtype).contiguous()
+        rank = lora_xa.shape[1]
+        if lora_b.shape != (out_features, rank):
+            raise ValueError(f"lora_b must be [{out_features}, {rank}], got {tuple(lora_b.shape)}")
+        lora_b = lora_b.contiguous()
+    lib = _lib.library()
+    rc = lib.moss_w8a16_gemm_fwd(
+        _lib.ptr(matrix), v_kind, rows, in_features,
+        _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), out_features,
+        _lib.ptr(bias), _lib.DTYPE_CODES.get(bias.dtype, -1) if bias is not None else 0,
+        _lib.ptr(lora_xa), _lib.ptr(lora_b), _lib.DTYPE_CODES.get(lora_b.dtype, -1) if lora_b is not None else 0,
+        rank, float(lora_scale),
+        _lib.ptr(output), _lib.DTYPE_CODES[output_dtype],
+        _lib.ptr(status_buffer(tokens.device)), _lib.stream_handle(tokens.device),
+    )
+    _lib.check(rc, "moss_w8a16_gemm_fwd")
+    return output.reshape(*tokens.shape[:-1], out_features)
+
+
+def int8_linear_backward(
+    gradient: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    input_shape: torch.Size,
+    input_dtype: torch.dtype,
+    weight_dtype: torch.dtype,
+    *,
+    out: torch.Tensor | None = None,
+    compute_dtype: torch.dtype | None = None,
+    lora_dyb: torch.Tensor | None = None,
+    lora_a: torch.Tensor | None = None,
+    lora_scale: float = 1.0,
+) -> torch.Tensor:
+    """dX = dY dec(W) (+ lora_scale * lora_dyb lora_a) on the sm_100a kernel.
+
+    Reference: ``triton_int8_linear_backward``, training/quant_kernels.py:337-373. The
+    product is rounded to the gradient's compute dtype and stored as ``input_dtype``.
+    The int8 weight is consumed in its ``[N, K]`` storage order (no transpose copy).
+    """
+    compute_dtype = gradient.dtype if compute_dtype is None else compute_dtype
+    v_kind = _compute_kind(compute_dtype)
+    matrix = gradient.reshape(-1, gradient.shape[-1])
+    if matrix.dtype != compute_dtype:
+        matrix = matrix.to(compute_dtype)
+    if not matrix.is_contiguous():
+        matrix = matrix.contiguous()
+    rows, out_features = matrix.shape
+    in_features = weight.shape[1]
+    if out is None:
+        grad_input = torch.empty((rows, in_features), device=gradient.device, dtype=input_dtype)
+    else:
+        grad_input = out.reshape(rows, in_features)
+        if grad_input.dtype != input_dtype or not grad_input.is_contiguous():
+            raise ValueError("int8 input-gradient buffer has the wrong dtype or is not contiguous.")
+    rank = 0
+    if lora_dyb is not None:
+        if lora_a is None:
+            raise ValueError("lora_dyb needs lora_a")
+        lora_dyb = lora_dyb.reshape(rows, -1)
+        if lora_dyb.dtype != compute_dtype or not lora_dyb.is_contiguous():
+            lora_dyb = lora_dyb.to(compute_dtype).contiguous()
+        rank = lora_dyb.shape[1]
+        if lora_a.shape != (rank, in_features):
+            raise ValueError(f"lora_a must be [{rank}, {in_features}], got {tuple(lora_a.shape)}")
+        lora_a = lora_a.contiguous()
+    lib = _lib.library()
+    rc = lib.moss_w8a16_gemm_dx(
+        _lib.ptr(matrix), v_kind, rows, out_features,
+        _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features,
+        _lib.ptr(lora_dyb), _lib.ptr(lora_a), _lib.DTYPE_CODES.get(lora_a.dtype, -1) if lora_a is not None else 0,
+        rank, float(lora_scale),
+        _lib.ptr(grad_input), _lib.dtype_code(input_dtype),
+        _lib.ptr(status_buffer(gradient.device)), _lib.stream_handle(gradient.device),
+    )
+    _lib.check(rc, "moss_w8a16_gemm_dx")
+    return grad_input.reshape(input_shape)
+
+
+# Reference launcher names (training/quant_kernels.py:294, :337): same contract, B200 kernel.
+triton_int8_linear_forward = int8_linear_forward
+triton_int8_linear_backward = int8_linear_backward
+
+
+def quantize_weight(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel symmetric int8 codes and f32 scales, bit-exact with the reference.
+
+    Reference: ``FrozenInt8Linear.__init__``, training/quantization.py:87-91. Runs on the
+    weight's CUDA device; a CPU weight is staged through the current CUDA device and the
+    results are returned on the weight's device. Raises ``ValueError`` for non-finite input.
+    """
+    if weight.ndim != 2:
+        raise ValueError("weight must be 2-D [out_features, in_features]")
+    if not torch.cuda.is_available():
+        raise RuntimeError("int8 quantization needs a CUDA device (the sm_100a quantiser has no CPU fallback).")
+    source_device = weight.device
+    work = weight.detach()
+    if work.device.type != "cuda":
+        work = work.to(torch.device("cuda", torch.cuda.current_device()))
+    if work.dtype not in _lib.DTYPE_CODES:
+        work = work.float()
+    work = work.contiguous()
+    n, k = work.shape
+    codes = torch.empty((n, k), dtype=torch.int8, device=work.device)
+    scale = torch.empty((n,), dtype=torch.float32, device=work.device)
+    status = torch.zeros(1, dtype=torch.int32, device=work.device)
+    rc = _lib.library().moss_w8_quantize(
+        _lib.ptr(work), _lib.DTYPE_CODES[work.dtype], n, k, _lib.ptr(codes), _lib.ptr(scale),
+        _lib.ptr(status), _lib.stream_handle(work.device),
+    )
+    _lib.check(rc, "moss_w8_quantize")
+    if int(status.item()) & _lib.STATUS_NONFINITE_WEIGHT:
+        raise ValueError("Cannot quantize non-finite linear weights.")
+    if source_device != work.device:
+        codes = codes.to(source_device)
+        scale = scale.to(source_device)
+    return codes, scale
+
+
+def dequantize_weight(weight: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Transient decoded weight ``round_d(q * round_d(s))`` (reference quantization.py:23-24)."""
+    if weight.device.type != "cuda":
+        raise RuntimeError("int8 quantized backend is unavailable: the weight is not on CUDA.")
+    out = torch.empty(weight.shape, dtype=dtype, device=weight.device)
+    rc = _lib.library().moss_w8_dequantize(
+        _lib.ptr(weight), _lib.ptr(scale), weight.shape[0], weight.shape[1], _lib.dtype_code(dtype),
+        _lib.ptr(out), _lib.stream_handle(weight.device),
+    )
+    _lib.check(rc, "moss_w8_dequantize")
+    return out
