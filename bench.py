@@ -1,0 +1,462 @@
+"""Benchmark of the int8 weight-only DiT LoRA training step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the per-GPU shape of the benchmark's 1/2/4/8-GPU configuration): a 36-block
+synthetic DiT (width 3072, 24 heads x 128, MLP 3072 -> 12288 -> 3072 GELU, per-block adaLN
+3072 -> 18432), every linear int8 weight-only, LoRA rank 32 on q/k/v/o, batch 2 x (4096
+image + 512 text) tokens per GPU, bf16 autocast, gradient checkpointing per block, saved
+activations offloaded to the pinned-host ring, AdamW on the adapters, and (N > 1) a
+bucketed NCCL all-reduce of the adapter gradients. One "step" is one such training step.
+
+Rank 0 prints one JSON line: whole-job tokens/s with inputs resident in HBM (``value``),
+the same through host buffers (``e2e``), the roofline of the dominant kernel (the int8
+GEMM, every launch timed with CUDA events inside the timed region), the CPU baseline
+(the reference's CPU algorithm restated in ``oracle/``, timed on this host), SM clocks
+sampled during the timed region, and the number of this library's kernel launches.
+
+``--impl reference`` times the reference's CPU implementation of the same step (rank 0
+only) and prints the same kind of line with ``"impl": "reference"``.
+``--kernel gemm_fwd|gemm_dx --m M --k K --n N`` runs only the int8 GEMM (profiling aid).
+``--sweep`` runs the GEMM sweep (M x (K, N) grid) and prints one JSON line per case.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+METRIC = "INT8-W DiT train tokens/s at 1/2/4/8 B200; W8 GEMM TFLOP/s; offload GB/s"
+IMG_TOKENS, TXT_TOKENS, DIM, HEADS, MLP, DEPTH, BATCH, RANK = 4096, 512, 3072, 24, 12288, 36, 2, 32
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=8)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--depth", type=int, default=DEPTH)
+    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--no-offload", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx"], default=None)
+    p.add_argument("--m", type=int, default=9216)
+    p.add_argument("--k", type=int, default=3072)
+    p.add_argument("--n", type=int, default=3072)
+    p.add_argument("--sweep", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: str) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s, p in zip(sm, power) if p > 0.3 * max(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ----------------------------------------------------------------------------- GEMM timing
+class GemmTimer:
+    """Launch observer: CUDA events around every int8 GEMM launch on its stream."""
+
+    def __init__(self) -> None:
+        import torch
+
+        self.torch = torch
+        self.records: list[tuple[str, int, int, int, object, object]] = []
+        self.active = False
+
+    def __call__(self, kind, m, n, k, device):
+        if not self.active:
+            return None
+        torch = self.torch
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        stream = torch.cuda.current_stream(device)
+        start.record(stream)
+
+        def done():
+            end.record(stream)
+            self.records.append((kind, m, n, k, start, end))
+
+        return done
+
+    def summary(self) -> dict:
+        out = {}
+        for kind in ("fwd", "dx"):
+            recs = [r for r in self.records if r[0] == kind]
+            if not recs:
+                continue
+            total_ms = sum(r[4].elapsed_time(r[5]) for r in recs)
+            flops = sum(2.0 * r[1] * r[2] * r[3] for r in recs)
+            bytes_ = sum(r[2] * r[3] + 4 * r[2] + 2 * r[1] * r[3] + 2 * r[1] * r[2] for r in recs)
+            out[kind] = {"launches": len(recs), "total_ms": total_ms, "flops": flops, "bytes": bytes_,
+                         "avg_us": 1e3 * total_ms / len(recs)}
+        return out
+
+
+def load_traffic(kind: str) -> float | None:
+    path = REPO / "profiles" / f"w8a16_gemm_{kind}_traffic.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["traffic_bytes_per_launch_at_bench_shape"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline_sample(reps: int = 1) -> dict:
+    sys.path.insert(0, str(REPO))
+    from oracle import cpu_step
+
+    seq = IMG_TOKENS + TXT_TOKENS
+    result = cpu_step.time_block_sample(dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seq=seq, reps=reps, warmup=1)
+    per_block = statistics.median(result["seconds"])
+    value = seq / (per_block * DEPTH)  # tokens/s of the full 36-block step, per sample
+    return {"value": value, "unit": "tokens/s", "cores": result["threads"], "kind": "port",
+            "sample": (f"1 of {DEPTH} blocks x 1 sample ({seq} tokens), checkpointed fwd + recompute + bwd, "
+                       f"median of {reps} after 1 warm-up, extrapolated x{DEPTH}; cpu={cpu_step.cpu_model_name()}"),
+            "seconds_per_block_sample": per_block}
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(REPO))
+    from oracle import cpu_step
+
+    seq = IMG_TOKENS + TXT_TOKENS
+    steps = max(1, args.steps)
+    result = cpu_step.time_block_sample(dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seq=seq,
+                                        reps=steps, warmup=min(args.warmup, 1))
+    per_block = statistics.median(result["seconds"])
+    value = seq / (per_block * DEPTH)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": per_block * DEPTH * args.batch * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "reference CPU path (oracle port) of the 36-block int8 LoRA step, batch 2 x 4608 tokens",
+                   "global_batch": args.batch, "seq_len": seq, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": result["threads"], "kind": "port",
+                         "sample": f"each step: 1 of {DEPTH} blocks x 1 sample, checkpointed fwd + recompute + bwd, "
+                                   f"extrapolated x{DEPTH}; cpu={cpu_step.cpu_model_name()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- kernel-only modes
+def run_kernel(args: argparse.Namespace) -> None:
+    import torch
+
+    from moss_image_b200 import quant_kernels as qk
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    m, k, n = args.m, args.k, args.n
+    gen = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(n, k, device=dev, generator=gen) * 0.02
+    q, s = qk.quantize_weight(w)
+    del w
+    if args.kernel == "gemm_fwd":
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        fn = lambda: qk.int8_linear_forward(x, q, s, None, torch.bfloat16, torch.bfloat16)  # noqa: E731
+    else:
+        dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
+        fn = lambda: qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)  # noqa: E731
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    qk.check_device_status(dev)
+    print(json.dumps({"kernel": args.kernel, "m": m, "k": k, "n": n, "us": ms * 1e3,
+                      "tflops": 2.0 * m * n * k / ms / 1e9}), flush=True)
+
+
+def run_sweep(args: argparse.Namespace) -> None:
+    import torch
+
+    from moss_image_b200 import quant_kernels as qk
+
+    peaks, _ = measured_peaks()
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for kn in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072), (3072, 18432)]:
+        k, n = kn
+        gen = torch.Generator(device=dev).manual_seed(0)
+        w = torch.randn(n, k, device=dev, generator=gen) * 0.02
+        q, s = qk.quantize_weight(w)
+        del w
+        for m in (128, 512, 2048, 8192, 32768):
+            x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+            dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
+            res = {"m": m, "k": k, "n": n}
+            for kind in ("fwd", "dx"):
+                if kind == "fwd":
+                    fn = lambda: qk.int8_linear_forward(x, q, s, None, torch.bfloat16, torch.bfloat16)  # noqa: E731
+                else:
+                    fn = lambda: qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16,  # noqa: E731
+                                                         torch.bfloat16)
+                for _ in range(3):
+                    fn()
+                times = []
+                for _ in range(max(3, args.steps)):
+                    flush.zero_()  # evict L2 between timed launches
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    fn()
+                    b.record()
+                    b.synchronize()
+                    times.append(a.elapsed_time(b))
+                ms = statistics.median(times)
+                flops = 2.0 * m * n * k
+                nbytes = n * k + 4 * n + 2 * m * k + 2 * m * n
+                t_roof = max(flops / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9))
+                res[kind] = {"us": ms * 1e3, "tflops": flops / ms / 1e9, "gbs": nbytes / ms / 1e6,
+                             "roofline_frac": t_roof / (ms * 1e-3)}
+            del x, dy
+            print(json.dumps(res), flush=True)
+    qk.check_device_status(dev)
+
+
+# ----------------------------------------------------------------------------- training step
+def run_train(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(REPO))
+    from moss_image_b200 import activation_offload as ao
+    from moss_image_b200 import quant_kernels as qk
+    from moss_image_b200.dit import build_lora_model, flow_matching_loss
+    from moss_image_b200.dp import GradAllReducer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0)
+    model.train()
+    model.activation_offload = not args.no_offload
+    params = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    reducer = GradAllReducer(params)
+
+    seq = IMG_TOKENS + TXT_TOKENS
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    latents = torch.randn(args.batch, IMG_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    text = torch.randn(args.batch, TXT_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    noise = torch.randn(args.batch, IMG_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    t = torch.rand(args.batch, device=dev, generator=gen)
+    host = [x.cpu().pin_memory() for x in (latents, text, noise, t)]
+    h2d_bytes = sum(x.numel() * x.element_size() for x in host)
+
+    def step(inputs) -> torch.Tensor:
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = flow_matching_loss(model, *inputs)
+        loss.backward()
+        reducer.finish()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+    inputs = (latents, text, t, noise)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(inputs)
+    qk.check_device_status(dev)
+    ring = ao.offload_ring(dev)
+    stats0 = ring.stats()
+
+    timer = GemmTimer()
+    qk.set_launch_observer(timer)
+    props = torch.cuda.get_device_properties(dev)
+    clocks = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+    barrier()
+    clocks.start()
+    timer.active = True
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step(inputs)
+    end.record()
+    barrier()
+    timer.active = False
+    clock_info = clocks.stop()
+    elapsed_ms = start.elapsed_time(end)
+    stats1 = ring.stats()
+    gemm = timer.summary()
+
+    # e2e: inputs copied from pinned host buffers each step, loss read back each step
+    dev_bufs = [torch.empty_like(x, device=dev) for x in host]
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    losses = []
+    for _ in range(args.steps):
+        for d, h in zip(dev_bufs, host):
+            d.copy_(h, non_blocking=True)
+        loss = step((dev_bufs[0], dev_bufs[1], dev_bufs[3], dev_bufs[2]))
+        losses.append(float(loss.item()))
+    e_end.record()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+    qk.check_device_status(dev)
+
+    times = torch.tensor([elapsed_ms, e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(times[0]), float(times[1])
+    tokens = world * args.batch * seq * args.steps
+    value = tokens / (elapsed_ms / 1e3)
+    e2e_value = tokens / (e2e_ms / 1e3)
+
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        dominant = max(gemm, key=lambda kind: gemm[kind]["total_ms"]) if gemm else None
+        roofline = None
+        if dominant is not None:
+            d = gemm[dominant]
+            per_launch_flops = d["flops"] / d["launches"]
+            achieved = per_launch_flops / (d["avg_us"] * 1e-6) / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            traffic = load_traffic(dominant)
+            roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak, "traffic": traffic,
+                        "kernel": f"w8a16_gemm_{dominant}", "peak_source": f"bf16_tflops_sustained ({peak_kind})",
+                        "launches_timed": d["launches"], "avg_launch_us": d["avg_us"],
+                        "algorithmic_flops_per_launch": per_launch_flops,
+                        "algorithmic_bytes_per_launch": d["bytes"] / d["launches"]}
+        offload_bytes = (stats1["d2h_bytes"] - stats0["d2h_bytes"]) + (stats1["h2d_bytes"] - stats0["h2d_bytes"])
+        gemm_tflops = {k: v["flops"] / (v["total_ms"] * 1e-3) / 1e12 for k, v in gemm.items()}
+        launches = sum(v["launches"] for v in gemm.values())
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": (f"{args.depth}-block synthetic DiT int8-W LoRA training step per GPU (batch "
+                                    f"{args.batch} x ({IMG_TOKENS} img + {TXT_TOKENS} txt) tokens, width {DIM}, MLP {MLP} "
+                                    f"GELU, per-block adaLN {DIM}->{6 * DIM}, LoRA r{RANK} q/k/v/o, grad checkpointing, "
+                                    f"activation offload {'on' if model.activation_offload else 'off'})"),
+                       "global_batch": world * args.batch, "seq_len": seq, "parallelism": f"dp{world}",
+                       "l2": "no flush: per-step working set (GBs of weights/activations) exceeds the 126 MB L2"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d_bytes,
+                    "d2h_bytes_per_step": 4},
+            "roofline": roofline,
+            "gemm_tflops": gemm_tflops,
+            "offload": {"bytes_per_step": offload_bytes / args.steps,
+                        "gbs_over_step": offload_bytes / (elapsed_ms * 1e-3) / 1e9,
+                        "pinned_bytes": stats1["pinned_bytes"]},
+            "clocks": clock_info,
+            "gpu_launches": launches,
+            "gpu_launches_note": "int8 GEMM launches (fwd + dx) of libmoss_w8.so in the timed region",
+            "loss_last": losses[-1] if losses else None,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample()
+        print(json.dumps(line), flush=True)
+    qk.set_launch_observer(None)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    elif args.kernel:
+        run_kernel(args)
+    elif args.sweep:
+        run_sweep(args)
+    else:
+        run_train(args)
+
+
+if __name__ == "__main__":
+    main()

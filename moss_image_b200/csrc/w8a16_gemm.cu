@@ -680,7 +680,7 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
       return fail(MOSS_ERR_INVALID_ARGUMENT, "LoRA operands need rank in [1, 256] and both factors");
   }
   if (M == 0 || Nc == 0) return clear_ok();
-  if (out == nullptr || a_ptr == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  if (out == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null output pointer");
   if (Kr == 0 && ext_a == nullptr) {
     const int64_t total = M * Nc;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4096));
@@ -689,7 +689,8 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
     MOSS_CUDA_TRY(cudaGetLastError());
     return clear_ok();
   }
-  if (q == nullptr || scale == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null weight or scale pointer");
+  if (Kr > 0 && (a_ptr == nullptr || q == nullptr || scale == nullptr))
+    return fail(MOSS_ERR_INVALID_ARGUMENT, "null input, weight or scale pointer");
 
   Args a{};
   a.M = static_cast<int>(M);

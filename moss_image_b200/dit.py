@@ -1,0 +1,184 @@
+"""Synthetic DiT block and block stack that host the int8 hot path (benchmark harness).
+
+The shapes follow the benchmark configuration of this path: width 3072, 24 heads x 128,
+joint attention over image + text tokens, MLP 3072 -> 12288 -> 3072 with GELU, and a
+per-block adaLN modulation linear 3072 -> 6 x 3072. The block mirrors the structure of the
+reference ``Block._forward_impl`` (training/model.py:269-314): RMSNorm + scale/shift
+modulation, q/k/v projections with per-head RMSNorm on q and k, joint attention, gated
+residual, modulated MLP with a gated residual. Every linear is a
+:class:`~moss_image_b200.quantization.FrozenInt8Linear`; q/k/v/o carry LoRA adapters.
+
+The stack wraps its forward in :func:`activation_cpu_offload` and checkpoints each block
+(non-reentrant), as the reference trainer does with ``grad_checkpointing: true``
+(training/model.py:687-709), so the offloaded tensors are the block inputs.
+Attention uses torch's scaled-dot-product attention (library code; not part of this path).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+from torch.utils.checkpoint import checkpoint
+
+from .activation_offload import activation_cpu_offload
+from .lora import LoRALinear
+from .quantization import quantize_frozen_linears
+
+
+class RMSNorm(nn.Module):
+    """Root-mean-square norm with a learned gain (training/model.py RMSNorm semantics)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dtype = x.dtype
+        h = x.float()
+        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.eps)
+        return (h * self.weight.float()).to(dtype)
+
+
+class SyntheticBlock(nn.Module):
+    """One joint attention + MLP block with its own adaLN modulation linear."""
+
+    def __init__(self, dim: int = 3072, heads: int = 24, mlp_dim: int = 12288) -> None:
+        super().__init__()
+        self.dim = dim
+        self.heads = heads
+        self.norm1 = RMSNorm(dim)
+        self.norm2 = RMSNorm(dim)
+        self.q_norm = RMSNorm(dim // heads)
+        self.k_norm = RMSNorm(dim // heads)
+        self.proj = nn.ModuleDict({name: nn.Linear(dim, dim, bias=False) for name in ("q", "k", "v", "o")})
+        self.mlp_up = nn.Linear(dim, mlp_dim, bias=True)
+        self.mlp_down = nn.Linear(mlp_dim, dim, bias=True)
+        self.adaln = nn.Linear(dim, 6 * dim, bias=True)
+
+    def forward(self, tokens: torch.Tensor, cond: torch.Tensor) -> torch.Tensor:
+        """tokens: [B, T, dim]; cond: [B, dim] (timestep embedding)."""
+        batch, seq, dim = tokens.shape
+        modulation = self.adaln(F.silu(cond)).view(batch, 6, dim)
+        shift_a, scale_a, gate_a, shift_f, scale_f, gate_f = (m.unsqueeze(1) for m in modulation.unbind(1))
+        h = self.norm1(tokens) * (1 + scale_a) + shift_a
+        q = self.q_norm(self.proj["q"](h).unflatten(-1, (self.heads, -1)))
+        k = self.k_norm(self.proj["k"](h).unflatten(-1, (self.heads, -1)))
+        v = self.proj["v"](h).unflatten(-1, (self.heads, -1))
+        attended = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+        attended = attended.transpose(1, 2).flatten(2)
+        tokens = tokens + self.proj["o"](attended) * gate_a
+        h = self.norm2(tokens) * (1 + scale_f) + shift_f
+        return tokens + self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")) * gate_f
+
+
+class TimestepEmbedding(nn.Module):
+    """Sinusoidal flow-matching time embedding followed by a small MLP (kept in fp32)."""
+
+    def __init__(self, dim: int, freq_dim: int = 256) -> None:
+        super().__init__()
+        self.freq_dim = freq_dim
+        self.mlp = nn.Sequential(nn.Linear(freq_dim, dim), nn.SiLU(), nn.Linear(dim, dim))
+
+    def forward(self, t: torch.Tensor) -> torch.Tensor:
+        half = self.freq_dim // 2
+        freqs = torch.exp(-math.log(10000.0) * torch.arange(half, device=t.device, dtype=torch.float32) / half)
+        phase = (1000.0 * t.float())[:, None] * freqs[None]
+        emb = torch.cat((phase.cos(), phase.sin()), -1)
+        return self.mlp(emb.to(self.mlp[0].weight.dtype))
+
+
+class SyntheticDiT(nn.Module):
+    """Stack of synthetic blocks with checkpointing and saved-activation offload."""
+
+    def __init__(self, depth: int = 36, dim: int = 3072, heads: int = 24, mlp_dim: int = 12288,
+                 gradient_checkpointing: bool = True) -> None:
+        super().__init__()
+        self.time_embedding = TimestepEmbedding(dim)
+        self.layers = nn.ModuleList(SyntheticBlock(dim, heads, mlp_dim) for _ in range(depth))
+        self.final_norm = RMSNorm(dim)
+        self.gradient_checkpointing = gradient_checkpointing
+        self.activation_offload = False
+
+    def forward(self, tokens: torch.Tensor, timestep: torch.Tensor) -> torch.Tensor:
+        with activation_cpu_offload(self, self.activation_offload, tokens.device):
+            cond = self.time_embedding(timestep).to(tokens.dtype)
+            for layer in self.layers:
+                if self.gradient_checkpointing and self.training and torch.is_grad_enabled():
+                    tokens = checkpoint(layer, tokens, cond, use_reentrant=False)
+                else:
+                    tokens = layer(tokens, cond)
+            return self.final_norm(tokens)
+
+
+def inject_lora(model: nn.Module, rank: int, alpha: float, targets: tuple[str, ...] = ("q", "k", "v", "o"),
+                a_std: float | None = 0.01) -> list[str]:
+    """Wrap the named projections of every block in :class:`LoRALinear`.
+
+    A ~ N(0, a_std) (the benchmark's adapter init; ``None`` keeps the reference's Kaiming
+    init), B = 0. Returns the wrapped module paths.
+    """
+    names = []
+    for index, layer in enumerate(model.layers):
+        _inject_block(layer, rank, alpha, targets, a_std)
+        names.extend(f"layers.{index}.proj.{name}" for name in targets)
+    return names
+
+
+def _inject_block(layer: SyntheticBlock, rank: int, alpha: float, targets: tuple[str, ...],
+                  a_std: float | None) -> None:
+    for name in targets:
+        base = layer.proj[name]
+        wrapped = LoRALinear(base, rank, alpha).to(device=base.weight.device)
+        if a_std is not None:
+            with torch.no_grad():
+                wrapped.lora_A.normal_(0.0, a_std)
+        layer.proj[name] = wrapped
+
+
+def build_lora_model(depth: int, *, device: torch.device, dim: int = 3072, heads: int = 24, mlp_dim: int = 12288,
+                     rank: int = 32, alpha: float | None = None, seed: int = 0,
+                     dtype: torch.dtype = torch.bfloat16) -> SyntheticDiT:
+    """Random-init stack (weights ~ N(0, 0.02)), int8 base, LoRA on q/k/v/o.
+
+    Mirrors the trainer's order (training/train.py:577-589): build, cast, inject LoRA,
+    quantise the frozen linears - done block by block on the device so that the
+    full-precision weights of only one block exist at a time.
+    """
+    torch.manual_seed(seed)
+    alpha = float(rank if alpha is None else alpha)
+    model = SyntheticDiT(depth=0, dim=dim, heads=heads, mlp_dim=mlp_dim)
+    model.time_embedding.to(device=device, dtype=dtype)
+    model.final_norm.to(device=device, dtype=dtype)
+    model.requires_grad_(False)
+    quantize_frozen_linears(model.time_embedding)
+    layers = []
+    for _ in range(depth):
+        block = SyntheticBlock(dim, heads, mlp_dim).to(device=device)
+        with torch.no_grad():
+            for module in block.modules():
+                if isinstance(module, nn.Linear):
+                    module.weight.normal_(0.0, 0.02)
+                    if module.bias is not None:
+                        module.bias.zero_()
+        block.to(dtype=dtype)
+        block.requires_grad_(False)
+        _inject_block(block, rank, alpha, ("q", "k", "v", "o"), 0.01)
+        quantize_frozen_linears(block)
+        layers.append(block)
+    model.layers = nn.ModuleList(layers)
+    return model
+
+
+def flow_matching_loss(model: SyntheticDiT, latents: torch.Tensor, text: torch.Tensor, t: torch.Tensor,
+                       noise: torch.Tensor) -> torch.Tensor:
+    """Rectified-flow velocity loss on the image tokens (text tokens are conditioning)."""
+    sigma = t.view(-1, 1, 1).to(latents.dtype)
+    noisy = (1 - sigma) * latents + sigma * noise
+    tokens = torch.cat((noisy, text), dim=1)
+    pred = model(tokens, t)[:, : latents.shape[1]]
+    target = noise - latents
+    return F.mse_loss(pred.float(), target.float())

@@ -25,6 +25,16 @@ _BACKENDS = {"auto", "eager", "triton"}
 
 _status_buffers: dict[tuple[str, int | None], torch.Tensor] = {}
 
+# Optional launch observer (benchmarks): called as observer(kind, m, n, k, device) before a
+# GEMM launch and returns a callable invoked right after it.
+_launch_observer = None
+
+
+def set_launch_observer(observer) -> None:
+    """Install (or clear with ``None``) a callback wrapped around every GEMM launch."""
+    global _launch_observer
+    _launch_observer = observer
+
 
 def validate_quantized_backend(backend: str) -> QuantizedBackend:
     """Reference: training/quant_kernels.py:30-33 (same accepted strings and message)."""
@@ -130,7 +140,10 @@ def _compute_kind(dtype: torch.dtype) -> int:
 
 
 def _matrix_view(tokens: torch.Tensor) -> torch.Tensor:
-    return tokens.reshape(-1, tokens.shape[-1])
+    rows = 1
+    for size in tokens.shape[:-1]:
+        rows *= size
+    return tokens.reshape(rows, tokens.shape[-1])
 
 
 def int8_linear_forward(
@@ -180,6 +193,7 @@ def int8_linear_forward(
             raise ValueError(f"lora_b must be [{out_features}, {rank}], got {tuple(lora_b.shape)}")
         lora_b = lora_b.contiguous()
     lib = _lib.library()
+    done = _launch_observer("fwd", rows, out_features, in_features, tokens.device) if _launch_observer else None
     rc = lib.moss_w8a16_gemm_fwd(
         _lib.ptr(matrix), v_kind, rows, in_features,
         _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), out_features,
@@ -189,6 +203,8 @@ def int8_linear_forward(
         _lib.ptr(output), _lib.DTYPE_CODES[output_dtype],
         _lib.ptr(status_buffer(tokens.device)), _lib.stream_handle(tokens.device),
     )
+    if done is not None:
+        done()
     _lib.check(rc, "moss_w8a16_gemm_fwd")
     return output.reshape(*tokens.shape[:-1], out_features)
 
@@ -215,7 +231,7 @@ def int8_linear_backward(
     """
     compute_dtype = gradient.dtype if compute_dtype is None else compute_dtype
     v_kind = _compute_kind(compute_dtype)
-    matrix = gradient.reshape(-1, gradient.shape[-1])
+    matrix = _matrix_view(gradient)
     if matrix.dtype != compute_dtype:
         matrix = matrix.to(compute_dtype)
     if not matrix.is_contiguous():
@@ -240,6 +256,7 @@ def int8_linear_backward(
             raise ValueError(f"lora_a must be [{rank}, {in_features}], got {tuple(lora_a.shape)}")
         lora_a = lora_a.contiguous()
     lib = _lib.library()
+    done = _launch_observer("dx", rows, in_features, out_features, gradient.device) if _launch_observer else None
     rc = lib.moss_w8a16_gemm_dx(
         _lib.ptr(matrix), v_kind, rows, out_features,
         _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features,
@@ -248,6 +265,8 @@ def int8_linear_backward(
         _lib.ptr(grad_input), _lib.dtype_code(input_dtype),
         _lib.ptr(status_buffer(gradient.device)), _lib.stream_handle(gradient.device),
     )
+    if done is not None:
+        done()
     _lib.check(rc, "moss_w8a16_gemm_dx")
     return grad_input.reshape(input_shape)
 
