@@ -42,7 +42,7 @@ def test_forward_backward_and_saved_storage(cuda_device):
     gradient = torch.randn_like(actual)
     actual.backward(gradient)
     expected.backward(gradient.float())
-    torch.testing.assert_close(tokens.grad.float(), reference.grad, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(tokens.grad.float(), reference.grad.float(), atol=2e-2, rtol=2e-2)
     assert len(saved) == 2
     assert saved[0].dtype == torch.int8
     assert saved[1].shape == (32,)
