@@ -1,0 +1,141 @@
+// int8 -> 16-bit operand decode shared by the GEMM kernels, plus small shared-memory helpers.
+//
+// Decode rounding follows training/quant_kernels.py:138-149 (and the eager
+// training/quantization.py:23-24): dec = round_v(round_w(q * round_w(s))), with v the compute
+// dtype and w the module (weight) dtype.
+#pragma once
+
+#include "common.cuh"
+
+namespace moss {
+namespace gemm {
+
+// int8 -> 16-bit decode of one 32-bit word (4 codes) into two packed pairs.
+//
+// bf16: for a code q with raw byte b, A = bf16 bits 0x4300 | (b & 0x7F) = 128 + (b & 127) and
+// C = 0x4300 | (b & 0x80) = 128 or 256. A - C = q exactly (two's complement), then one
+// round-to-nearest bf16 multiply by bf16(s) gives bf16(q * bf16(s)) exactly as the reference.
+__device__ __forceinline__ void dequant_word_bf16(uint32_t w, __nv_bfloat162 s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t t01 = prmt(w, 0x43u, 0x4140u);  // 0x43 b1 0x43 b0
+  const uint32_t t23 = prmt(w, 0x43u, 0x4342u);
+  const uint32_t a01 = t01 & 0xFF7FFF7Fu, c01 = t01 & 0xFF80FF80u;
+  const uint32_t a23 = t23 & 0xFF7FFF7Fu, c23 = t23 & 0xFF80FF80u;
+  __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a01),
+                               *reinterpret_cast<const __nv_bfloat162*>(&c01));
+  __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a23),
+                               *reinterpret_cast<const __nv_bfloat162*>(&c23));
+  x01 = __hmul2(x01, s2);
+  x23 = __hmul2(x23, s2);
+  lo = *reinterpret_cast<uint32_t*>(&x01);
+  hi = *reinterpret_cast<uint32_t*>(&x23);
+}
+
+// f16: 0x6400 | (b ^ 0x80) is the half 1024 + q + 128 exactly; subtracting 1152 gives q.
+__device__ __forceinline__ void dequant_word_f16(uint32_t w, __half2 s2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t t01 = prmt(u, 0x64u, 0x4140u);
+  const uint32_t t23 = prmt(u, 0x64u, 0x4342u);
+  const __half2 magic = __half2half2(__ushort_as_half(0x6480));  // 1152
+  __half2 x01 = __hsub2(*reinterpret_cast<const __half2*>(&t01), magic);
+  __half2 x23 = __hsub2(*reinterpret_cast<const __half2*>(&t23), magic);
+  x01 = __hmul2(x01, s2);
+  x23 = __hmul2(x23, s2);
+  lo = *reinterpret_cast<uint32_t*>(&x01);
+  hi = *reinterpret_cast<uint32_t*>(&x23);
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, int v_kind) {
+  if (v_kind == kBF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 16 f32 values times s -> two 16-byte chunks of the 16-bit operand (LoRA factor blocks).
+__device__ __forceinline__ void pack16_scaled(const float (&f)[16], float s, int v_kind, uint4& o0, uint4& o1) {
+  o0 = make_uint4(pack2(f[0] * s, f[1] * s, v_kind), pack2(f[2] * s, f[3] * s, v_kind),
+                  pack2(f[4] * s, f[5] * s, v_kind), pack2(f[6] * s, f[7] * s, v_kind));
+  o1 = make_uint4(pack2(f[8] * s, f[9] * s, v_kind), pack2(f[10] * s, f[11] * s, v_kind),
+                  pack2(f[12] * s, f[13] * s, v_kind), pack2(f[14] * s, f[15] * s, v_kind));
+}
+
+// Load 16 consecutive values of a float-kind row as f32, zero past `ncols` (LoRA factors).
+__device__ __forceinline__ void load16_f32(const void* base, int kind, int64_t row_off, int col0, int ncols,
+                                           float (&v)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = col0 + i;
+    v[i] = (c < ncols) ? load_as_float(base, kind, row_off + c) : 0.0f;
+  }
+}
+
+// Generic decode (weight dtype differs from the compute dtype): f32 arithmetic.
+__device__ __forceinline__ void dequant_word_generic(uint32_t w, float s_w, int w_kind, int v_kind,
+                                                     uint32_t& lo, uint32_t& hi) {
+  float d[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float q = static_cast<float>(static_cast<int8_t>((w >> (8 * i)) & 0xFF));
+    d[i] = round_to_kind(q * s_w, w_kind);
+  }
+  lo = pack2(d[0], d[1], v_kind);
+  hi = pack2(d[2], d[3], v_kind);
+}
+
+// Per-row decode context (scale in the right representation for each path).
+template <int kV, bool kFast>
+struct Dec {
+  uint32_t s2;   // packed pair of round_v(s) for the fast paths
+  float s_w;     // round_w(s) for the generic path
+  __device__ __forceinline__ void set(float s, int w_kind) {
+    if constexpr (kFast) {
+      if constexpr (kV == kBF16) {
+        __nv_bfloat162 h = __bfloat162bfloat162(__float2bfloat16_rn(s));
+        s2 = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __half2half2(__float2half_rn(s));
+        s2 = *reinterpret_cast<uint32_t*>(&h);
+      }
+    } else {
+      s_w = round_to_kind(s, w_kind);
+    }
+  }
+  __device__ __forceinline__ void word(uint32_t w, int w_kind, uint32_t& lo, uint32_t& hi) const {
+    if constexpr (kFast) {
+      if constexpr (kV == kBF16) {
+        dequant_word_bf16(w, *reinterpret_cast<const __nv_bfloat162*>(&s2), lo, hi);
+      } else {
+        dequant_word_f16(w, *reinterpret_cast<const __half2*>(&s2), lo, hi);
+      }
+    } else {
+      dequant_word_generic(w, s_w, w_kind, kV, lo, hi);
+    }
+  }
+  // 16 codes -> 32 bytes of 16-bit operand
+  __device__ __forceinline__ void chunk(uint4 q, int w_kind, uint4& o0, uint4& o1) const {
+    word(q.x, w_kind, o0.x, o0.y);
+    word(q.y, w_kind, o0.z, o0.w);
+    word(q.z, w_kind, o1.x, o1.y);
+    word(q.w, w_kind, o1.z, o1.w);
+  }
+};
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+
+}  // namespace gemm
+}  // namespace moss

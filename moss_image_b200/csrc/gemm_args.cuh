@@ -1,0 +1,99 @@
+// Launch arguments shared by the int8 GEMM kernels (1-CTA and CTA-pair variants).
+#pragma once
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace moss {
+namespace gemm {
+
+struct Args {
+  int M, Nc, Kr;            // C[M, Nc] = A[M, Kr] * B[Kr, Nc]
+  int tiles_m, tiles_n;
+  int main_kb, num_kb;      // k-blocks from the int8 weight, total (incl. LoRA extension)
+  int manual;               // 1: producer uses plain loads (shapes TMA cannot describe)
+  const void* a; int64_t lda;
+  const int8_t* w; int64_t ldw; int w_rows, w_cols;
+  const float* scale;
+  int w_kind;
+  const void* bias; int bias_kind;
+  void* out; int out_kind; int64_t ldo;
+  const void* ext_a; int64_t ld_ext_a;             // LoRA: [M, r] (value dtype)
+  const void* ext_b; int ext_b_kind; int64_t ld_ext_b; int ext_r;  // fwd [Nc, r]; dx [r, Nc]
+  float ext_scale;
+  int* status;
+};
+
+// ------------------------------------------------------------------ host: TMA descriptors
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tiled tensor map of `rank` (2 or 3) dimensions: dims/box innermost first, strides in bytes
+// for dimensions 1.. . Returns false (no map) when TMA cannot describe the view.
+inline bool make_map_nd(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, int rank,
+                        const uint64_t* dims, const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr || rank < 2 || rank > 3) return false;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
+  if ((static_cast<uint64_t>(box[0]) * esize) % 16 != 0) return false;
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t bx[3];
+  cuuint32_t es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] == 0 || box[i] == 0 || box[i] > 256) return false;
+    d[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) {
+    if (strides[i] % 16 != 0) return false;
+    st[i] = strides[i];
+  }
+  return fn(map, dt, rank, const_cast<void*>(ptr), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, uint64_t inner,
+                     uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return make_map_nd(map, dt, esize, ptr, 2, dims, strides, box, swz);
+}
+
+// Grouped tile rasterisation: tiles are walked in groups of kGroupM row blocks x all column
+// blocks, so the tiles in flight at one time (one per CTA or CTA pair) cover a compact
+// block of the output and reuse their A rows and weight columns from L2.
+constexpr int kGroupM = 8;
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m_blk, int& n_blk) {
+  const int per_group = kGroupM * tiles_n;
+  const int group = t / per_group;
+  const int first_m = group * kGroupM;
+  const int gsm = min(tiles_m - first_m, kGroupM);
+  const int r = t - group * per_group;
+  m_blk = first_m + r % gsm;
+  n_blk = r / gsm;
+}
+
+// CTA-pair (cta_group::2) launcher, defined in w8a16_gemm_2sm.cu. Builds its own tensor maps;
+// returns MOSS_ERR_UNSUPPORTED (without launching) when the shapes do not fit it.
+int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t stream);
+
+}  // namespace gemm
+}  // namespace moss

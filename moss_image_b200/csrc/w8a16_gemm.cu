@@ -23,7 +23,9 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "dequant.cuh"
 #include "errors.cuh"
+#include "gemm_args.cuh"
 
 namespace moss {
 namespace gemm {
@@ -43,23 +45,9 @@ constexpr uint32_t kBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kDataBytes = kStages * (kABytes + kWBytes) + kBStages * kBBytes;
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 256;
-
-struct Args {
-  int M, Nc, Kr;            // C[M, Nc] = A[M, Kr] * B[Kr, Nc]
-  int tiles_m, tiles_n;
-  int main_kb, num_kb;      // k-blocks from the int8 weight, total (incl. LoRA extension)
-  int manual;               // 1: producer uses plain loads (shapes TMA cannot describe)
-  const void* a; int64_t lda;
-  const int8_t* w; int64_t ldw; int w_rows, w_cols;
-  const float* scale;
-  int w_kind;
-  const void* bias; int bias_kind;
-  void* out; int out_kind; int64_t ldo;
-  const void* ext_a; int64_t ld_ext_a;             // LoRA: [M, r] (value dtype)
-  const void* ext_b; int ext_b_kind; int64_t ld_ext_b; int ext_r;  // fwd [Nc, r]; dx [r, Nc]
-  float ext_scale;
-  int* status;
-};
+// Problems with more rows than this use the CTA-pair kernel (256-row tiles) when TMA can
+// describe them; smaller ones keep 128-row tiles.
+constexpr int64_t kPairMinRows = 128;
 
 struct Barriers {
   uint64_t full[kStages];
@@ -74,129 +62,10 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block too large");
 
-// --------------------------------------------------------------------------------------------
-// int8 -> 16-bit decode of one 32-bit word (4 codes) into two packed pairs.
-//
-// bf16: for a code q with raw byte b, A = bf16 bits 0x4300 | (b & 0x7F) = 128 + (b & 127) and
-// C = 0x4300 | (b & 0x80) = 128 or 256. A - C = q exactly (two's complement), then one
-// round-to-nearest bf16 multiply by bf16(s) gives bf16(q * bf16(s)) exactly as the reference.
-__device__ __forceinline__ void dequant_word_bf16(uint32_t w, __nv_bfloat162 s2, uint32_t& lo, uint32_t& hi) {
-  const uint32_t t01 = prmt(w, 0x43u, 0x4140u);  // 0x43 b1 0x43 b0
-  const uint32_t t23 = prmt(w, 0x43u, 0x4342u);
-  const uint32_t a01 = t01 & 0xFF7FFF7Fu, c01 = t01 & 0xFF80FF80u;
-  const uint32_t a23 = t23 & 0xFF7FFF7Fu, c23 = t23 & 0xFF80FF80u;
-  __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a01),
-                               *reinterpret_cast<const __nv_bfloat162*>(&c01));
-  __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a23),
-                               *reinterpret_cast<const __nv_bfloat162*>(&c23));
-  x01 = __hmul2(x01, s2);
-  x23 = __hmul2(x23, s2);
-  lo = *reinterpret_cast<uint32_t*>(&x01);
-  hi = *reinterpret_cast<uint32_t*>(&x23);
-}
-
-// f16: 0x6400 | (b ^ 0x80) is the half 1024 + q + 128 exactly; subtracting 1152 gives q.
-__device__ __forceinline__ void dequant_word_f16(uint32_t w, __half2 s2, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const uint32_t t01 = prmt(u, 0x64u, 0x4140u);
-  const uint32_t t23 = prmt(u, 0x64u, 0x4342u);
-  const __half2 magic = __half2half2(__ushort_as_half(0x6480));  // 1152
-  __half2 x01 = __hsub2(*reinterpret_cast<const __half2*>(&t01), magic);
-  __half2 x23 = __hsub2(*reinterpret_cast<const __half2*>(&t23), magic);
-  x01 = __hmul2(x01, s2);
-  x23 = __hmul2(x23, s2);
-  lo = *reinterpret_cast<uint32_t*>(&x01);
-  hi = *reinterpret_cast<uint32_t*>(&x23);
-}
-
-__device__ __forceinline__ uint32_t pack2(float a, float b, int v_kind) {
-  if (v_kind == kBF16) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Generic decode (weight dtype differs from the compute dtype): f32 arithmetic.
-__device__ __forceinline__ void dequant_word_generic(uint32_t w, float s_w, int w_kind, int v_kind,
-                                                     uint32_t& lo, uint32_t& hi) {
-  float d[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float q = static_cast<float>(static_cast<int8_t>((w >> (8 * i)) & 0xFF));
-    d[i] = round_to_kind(q * s_w, w_kind);
-  }
-  lo = pack2(d[0], d[1], v_kind);
-  hi = pack2(d[2], d[3], v_kind);
-}
-
-// Per-row decode context (scale in the right representation for each path).
-template <int kV, bool kFast>
-struct Dec {
-  uint32_t s2;   // packed pair of round_v(s) for the fast paths
-  float s_w;     // round_w(s) for the generic path
-  __device__ __forceinline__ void set(float s, int w_kind) {
-    if constexpr (kFast) {
-      if constexpr (kV == kBF16) {
-        __nv_bfloat162 h = __bfloat162bfloat162(__float2bfloat16_rn(s));
-        s2 = *reinterpret_cast<uint32_t*>(&h);
-      } else {
-        __half2 h = __half2half2(__float2half_rn(s));
-        s2 = *reinterpret_cast<uint32_t*>(&h);
-      }
-    } else {
-      s_w = round_to_kind(s, w_kind);
-    }
-  }
-  __device__ __forceinline__ void word(uint32_t w, int w_kind, uint32_t& lo, uint32_t& hi) const {
-    if constexpr (kFast) {
-      if constexpr (kV == kBF16) {
-        dequant_word_bf16(w, *reinterpret_cast<const __nv_bfloat162*>(&s2), lo, hi);
-      } else {
-        dequant_word_f16(w, *reinterpret_cast<const __half2*>(&s2), lo, hi);
-      }
-    } else {
-      dequant_word_generic(w, s_w, w_kind, kV, lo, hi);
-    }
-  }
-  // 16 codes -> 32 bytes of 16-bit operand
-  __device__ __forceinline__ void chunk(uint4 q, int w_kind, uint4& o0, uint4& o1) const {
-    word(q.x, w_kind, o0.x, o0.y);
-    word(q.y, w_kind, o0.z, o0.w);
-    word(q.z, w_kind, o1.x, o1.y);
-    word(q.w, w_kind, o1.z, o1.w);
-  }
-};
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-
 // Byte offset of element (row, col) of a 16-bit K-major SW128 tile (rows of 64 elements).
 __device__ __forceinline__ uint32_t sw128_kmajor_off16(int row, int col) {
   return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ (row & 7)) & 7) << 4) +
                                (col & 7) * 2);
-}
-
-// Load 16 consecutive values of a float-kind row as f32 with bounds (used for LoRA blocks).
-__device__ __forceinline__ void load16_f32(const void* base, int kind, int64_t row_off, int col0, int ncols,
-                                           float (&v)[16]) {
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int c = col0 + i;
-    v[i] = (c < ncols) ? load_as_float(base, kind, row_off + c) : 0.0f;
-  }
 }
 
 // --------------------------------------------------------------------------------------------
@@ -258,8 +127,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t last_phase_mask = 0;  // phase bit of the last copy per stage
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int m0 = (t % args.tiles_m) * BM;
-      const int n0 = (t / args.tiles_m) * BN;
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int m0 = m_blk * BM;
+      const int n0 = n_blk * BN;
       for (int kb = 0; kb < args.num_kb; ++kb) {
         if (!mbar_wait(bar(bars->empty[stage]), phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
           ok = false;
@@ -415,8 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_EPILOGUE))
         break;
       tc_fence_after();
-      const int m0 = (t % args.tiles_m) * BM;
-      const int n0 = (t / args.tiles_m) * BN;
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int m0 = m_blk * BM;
+      const int n0 = n_blk * BN;
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
       const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 7) == 0) &&
@@ -466,7 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0, bphase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int n0 = (t / args.tiles_m) * BN;
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int n0 = n_blk * BN;
       // forward: this thread always handles tile rows (ct >> 2) + 64 j, j = 0..3
       Dec<kV, kFast> dec_f[4];
       if constexpr (!kDX) {
@@ -504,14 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) f[i] = 0.0f;
               }
-              o0 = make_uint4(pack2(f[0] * args.ext_scale, f[1] * args.ext_scale, kV),
-                              pack2(f[2] * args.ext_scale, f[3] * args.ext_scale, kV),
-                              pack2(f[4] * args.ext_scale, f[5] * args.ext_scale, kV),
-                              pack2(f[6] * args.ext_scale, f[7] * args.ext_scale, kV));
-              o1 = make_uint4(pack2(f[8] * args.ext_scale, f[9] * args.ext_scale, kV),
-                              pack2(f[10] * args.ext_scale, f[11] * args.ext_scale, kV),
-                              pack2(f[12] * args.ext_scale, f[13] * args.ext_scale, kV),
-                              pack2(f[14] * args.ext_scale, f[15] * args.ext_scale, kV));
+              pack16_scaled(f, args.ext_scale, kV, o0, o1);
             }
             const uint32_t rbase = b_base + (row >> 3) * 1024 + (row & 7) * 128;
             sts128(rbase + ((((2 * c) ^ (row & 7)) & 7) << 4), o0);
@@ -548,14 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 16; ++i) f[i] = 0.0f;
               }
-              o0 = make_uint4(pack2(f[0] * args.ext_scale, f[1] * args.ext_scale, kV),
-                              pack2(f[2] * args.ext_scale, f[3] * args.ext_scale, kV),
-                              pack2(f[4] * args.ext_scale, f[5] * args.ext_scale, kV),
-                              pack2(f[6] * args.ext_scale, f[7] * args.ext_scale, kV));
-              o1 = make_uint4(pack2(f[8] * args.ext_scale, f[9] * args.ext_scale, kV),
-                              pack2(f[10] * args.ext_scale, f[11] * args.ext_scale, kV),
-                              pack2(f[12] * args.ext_scale, f[13] * args.ext_scale, kV),
-                              pack2(f[14] * args.ext_scale, f[15] * args.ext_scale, kV));
+              pack16_scaled(f, args.ext_scale, kV, o0, o1);
             }
             const uint32_t rbase = b_base + a * (kBBytes / 4) + row * 128;
             sts128(rbase + ((((2 * qd) ^ r_in) & 7) << 4), o0);
@@ -596,38 +457,6 @@ __global__ void fill_bias_kernel(int M, int N, const void* bias, int bias_kind, 
 
 // --------------------------------------------------------------------------------------------
 // host side
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, uint64_t inner,
-                     uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-                     CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = encode_fn();
-  if (fn == nullptr) return false;
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (row_bytes & 15) != 0) return false;
-  if ((static_cast<uint64_t>(box_inner) * esize) % 16 != 0) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 static int sm_count() {
   int dev = 0, n = 0;
@@ -741,6 +570,15 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
     tma = make_map(&te, v_dt, 2, ext_a, ext_r, M, ext_r * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
+  if (tma && M > kPairMinRows) {
+    // CTA-pair kernel: 256 x 256 tiles, multi-k-block TMA boxes; falls through when the
+    // shapes do not fit its boxes.
+    Args a2 = a;
+    a2.tiles_m = static_cast<int>((M + 255) / 256);
+    a2.tiles_n = static_cast<int>((Nc + 255) / 256);
+    const int rc = launch_pair(dx, v_kind, fast, a2, stream);
+    if (rc != MOSS_ERR_UNSUPPORTED) return rc;
+  }
   return dx ? dispatch<true>(v_kind, fast, ta, tw, te, a, stream) : dispatch<false>(v_kind, fast, ta, tw, te, a, stream);
 }
 

@@ -1,0 +1,619 @@
+// CTA-pair (cta_group::2) variant of the weight-only int8 GEMM for sm_100a.
+//
+// A cluster of two CTAs on two SMs computes one 256 x 256 output tile with 2-SM UMMAs
+// (tcgen05.mma.cta_group::2, M = 256, N = 256, K = 16):
+//   * each CTA TMA-loads its 128 rows of the bf16/f16 A tile into its own shared memory;
+//   * each CTA TMA-loads its 128-row half of the int8 weight tile into its own shared
+//     memory and its converter warps dequantise that half into the canonical SW128 layout;
+//     once both halves of a stage (A rows and converted B columns) are in place they signal
+//     the leader (remote mbarrier arrive through mapa);
+//   * the leader's single MMA thread issues the 2-SM MMAs; the hardware reads the A rows and
+//     B columns held by each CTA at the same shared-memory offsets, and each CTA's TMEM holds
+//     its 128 accumulator rows; completion is committed to both CTAs (multicast commit);
+//   * each CTA's epilogue warps drain their own TMEM half and release it to the leader.
+// Compared with the 1-CTA kernel this halves the dequant work per SM, lowers the operand
+// bytes per FLOP (each SM loads half of the int8 tile), and leaves room for 6 load stages.
+// The decode rounding is identical (dequant.cuh).
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "errors.cuh"
+#include "gemm_args.cuh"
+
+namespace moss {
+namespace gemm {
+namespace pair {
+
+constexpr int BK = 64;
+constexpr int kHalf = 128;  // rows of A (M) and of B (N) held by each CTA
+constexpr int kTileM = 256;
+constexpr int kTileN = 256;
+// TMA cost on this part is dominated by a per-operation overhead (about two tensor ops in
+// flight per SM), so each load stage fetches kSub k-blocks with one 3-D box per operand.
+constexpr int kSub = 2;
+constexpr int kStages = 3;
+constexpr int kBStages = 4;
+constexpr int kConvWarps = 8;
+constexpr int kEpiWarp0 = 4;
+constexpr int kConvWarp0 = 8;
+constexpr int kThreads = 16 * 32;
+constexpr uint32_t kABlock = kHalf * BK * 2;  // 16 KB: one k-block of this CTA's A rows
+constexpr uint32_t kWBlock = kHalf * BK;      // 8 KB: one k-block of this CTA's int8 half
+constexpr uint32_t kAStage = kSub * kABlock;
+constexpr uint32_t kWStage = kSub * kWBlock;
+constexpr uint32_t kBBytes = kHalf * BK * 2;  // 16 KB converted operand per k-block
+constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
+constexpr uint32_t kDataBytes = kStages * (kAStage + kWStage) + kBStages * kBBytes;
+constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
+
+// Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
+// LoRA k-block. Every role walks the same sequence.
+struct Step {
+  bool ext;
+  int first_kb;  // weight k-block (main) or LoRA block index (ext)
+  int nsub;
+};
+// `rot` rotates the order of the main steps of a tile: tiles in flight at the same time that
+// share A rows or weight columns then read different k-slices, so they do not all request
+// the same lines at once (the accumulation order differs per tile, not the result set).
+__device__ __forceinline__ Step step_of(int s, int main_kb, int rot) {
+  const int main_steps = (main_kb + kSub - 1) / kSub;
+  Step st;
+  if (s < main_steps) {
+    int r = s + rot;
+    if (r >= main_steps) r -= main_steps;
+    st.ext = false;
+    st.first_kb = r * kSub;
+    st.nsub = min(kSub, main_kb - st.first_kb);
+  } else {
+    st.ext = true;
+    st.first_kb = s - main_steps;
+    st.nsub = 1;
+  }
+  return st;
+}
+__device__ __forceinline__ int step_rotation(int t, int main_kb) {
+  const int main_steps = (main_kb + kSub - 1) / kSub;
+  return main_steps > 0 ? (t * 7) % main_steps : 0;
+}
+__device__ __forceinline__ int steps_per_tile(const Args& a) {
+  return (a.main_kb + kSub - 1) / kSub + (a.num_kb - a.main_kb);
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+struct Barriers {
+  uint64_t a_full[kStages];    // local: this CTA's A half landed
+  uint64_t w_full[kStages];    // local: this CTA's int8 half landed
+  uint64_t empty[kStages];     // local: A + W stage free (MMA commit + local converters)
+  uint64_t b_full[kBStages];   // leader: both CTAs' converted halves written
+  uint64_t b_empty[kBStages];  // local: converted stage free (MMA commit)
+  uint64_t acc_full[2];        // local: accumulator ready (MMA commit)
+  uint64_t acc_empty[2];       // leader: both CTAs drained the accumulator
+  uint64_t drain;              // leader: all MMAs retired
+  uint64_t exit_bar;           // local: peer finished
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Barriers) <= 512, "barrier block too large");
+
+template <bool kDX, int kV, bool kFast>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
+                        const __grid_constant__ CUtensorMap tm_ext, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw_base);
+  const uint32_t a_smem = base;
+  const uint32_t w_smem = base + kStages * kAStage;
+  const uint32_t b_smem = w_smem + kStages * kWStage;
+  Barriers* bars = reinterpret_cast<Barriers*>(base_ptr + kDataBytes);
+  auto bar = [&](uint64_t& b) { return smem_u32(&b); };
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int nsteps = steps_per_tile(args);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(bars->a_full[s]), 1);
+      mbar_init(bar(bars->w_full[s]), 1);
+      mbar_init(bar(bars->empty[s]), 1 + kConvWarps);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(bar(bars->b_full[s]), 2 * kConvWarps);
+      mbar_init(bar(bars->b_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(bars->acc_full[s]), 1);
+      mbar_init(bar(bars->acc_empty[s]), 8);
+    }
+    mbar_init(bar(bars->drain), 1);
+    mbar_init(bar(bars->exit_bar), 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  // Both CTAs' barriers must be initialised before any cross-CTA arrival.
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_w);
+      if (args.ext_r > 0) tma_prefetch_desc(&tm_ext);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used_mask = 0, last_phase_mask = 0;
+    bool ok = true;
+    for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
+      const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
+      const int rot = step_rotation(t, args.main_kb);
+      for (int si = 0; si < nsteps; ++si) {
+        const Step st = step_of(si, args.main_kb, rot);
+        if (!mbar_wait_cluster(bar(bars->empty[stage]), phase ^ 1u, abort_flag, args.status,
+                               MOSS_STATUS_TIMEOUT_LOAD)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t a_dst = a_smem + stage * kAStage;
+          const uint32_t w_dst = w_smem + stage * kWStage;
+          const uint32_t a_bar = bar(bars->a_full[stage]);
+          const uint32_t w_bar = bar(bars->w_full[stage]);
+          if (!st.ext) {
+            // one op per operand for kSub k-blocks (chunks past K are zero-filled)
+            mbar_arrive_expect_tx(a_bar, kAStage);
+            tma_load_3d(a_dst, &tm_a, a_bar, 0, m0, st.first_kb);
+            mbar_arrive_expect_tx(w_bar, kWStage);
+            if constexpr (!kDX) {
+              tma_load_3d(w_dst, &tm_w, w_bar, 0, n0, st.first_kb);
+            } else {
+              tma_load_2d(w_dst, &tm_w, w_bar, n0, st.first_kb * BK);
+            }
+          } else {
+            mbar_arrive_expect_tx(a_bar, kABlock);
+            tma_load_2d(a_dst, &tm_ext, a_bar, st.first_kb * BK, m0);
+            mbar_arrive(w_bar);  // LoRA block: no int8 data, keep the phase
+          }
+          used_mask |= 1u << stage;
+          last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Drain our own copies before leaving.
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        if (!((used_mask >> s) & 1u)) continue;
+        const uint32_t ph = (last_phase_mask >> s) & 1u;
+        const long long start = clock64();
+        while (!mbar_try_wait(bar(bars->w_full[s]), ph) || !mbar_try_wait(bar(bars->a_full[s]), ph)) {
+          if (clock64() - start > kWaitBudgetCycles) {
+            report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (leader) {
+      constexpr uint32_t idesc = umma_idesc_f16(kV == kBF16 ? 1u : 0u, kDX, kTileM, kTileN);
+      int stage = 0, bstage = 0;
+      uint32_t phase = 0, bphase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = pair_id; t < num_tiles && ok; t += num_pairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait_cluster(bar(bars->acc_empty[acc]), acc_phase ^ 1u, abort_flag, args.status,
+                               MOSS_STATUS_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
+        bool first = true;
+        const int rot = step_rotation(t, args.main_kb);
+        for (int si = 0; si < nsteps && ok; ++si) {
+          const Step st = step_of(si, args.main_kb, rot);
+          if (!mbar_wait_cluster(bar(bars->a_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          for (int sub = 0; sub < st.nsub; ++sub) {
+            if (!mbar_wait_cluster(bar(bars->b_full[bstage]), bphase, abort_flag, args.status,
+                                   MOSS_STATUS_TIMEOUT_MMA)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+              const uint32_t a_base = a_smem + stage * kAStage + sub * kABlock;
+              const uint32_t b_base = b_smem + bstage * kBBytes;
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                const uint64_t adesc = umma_desc_sw128(a_base + kk * 32, 16, 1024);
+                uint64_t bdesc;
+                if constexpr (!kDX) {
+                  bdesc = umma_desc_sw128(b_base + kk * 32, 16, 1024);
+                } else {
+                  bdesc = umma_desc_sw128(b_base + kk * 2048, 8192, 1024);
+                }
+                umma_f16_pair(d_tmem, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
+              }
+              umma_commit_pair_mc(bar(bars->b_empty[bstage]), 0x3);
+              issued_any = true;
+            }
+            first = false;
+            __syncwarp();
+            if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
+          }
+          if (!ok) break;
+          if (lane == 0) umma_commit_pair_mc(bar(bars->empty[stage]), 0x3);
+          __syncwarp();
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        if (lane == 0) umma_commit_pair_mc(bar(bars->acc_full[acc]), 0x3);
+        __syncwarp();
+      }
+      if (lane == 0 && issued_any) {
+        umma_commit_pair(bar(bars->drain));
+        const long long start = clock64();
+        while (!mbar_try_wait(bar(bars->drain), 0)) {
+          if (clock64() - start > kWaitBudgetCycles) {
+            report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
+            break;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    int it = 0;
+    for (int t = pair_id; t < num_tiles; t += num_pairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_cluster(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status,
+                             MOSS_STATUS_TIMEOUT_EPILOGUE))
+        break;
+      tc_fence_after();
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
+      const int n0 = n_blk * kTileN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 7) == 0) &&
+                          ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               static_cast<uint32_t>(acc * kTileN + c * 32),
+                           r);
+        tmem_wait_ld();
+        if (c == kTileN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t eb = bar(bars->acc_empty[acc]);
+            if (leader)
+              mbar_arrive(eb);
+            else
+              mbar_arrive_cluster(mapa_shared(eb, 0));
+          }
+        }
+        const int col0 = n0 + c * 32;
+        if (col0 >= args.Nc) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(r[j]);
+          if constexpr (!kDX) {
+            if (args.bias != nullptr && col0 + j < args.Nc)
+              x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+          }
+          v[j] = round_to_kind(x, kV);
+        }
+        if (!row_ok) continue;
+        const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
+        if (vec_ok && col0 + 32 <= args.Nc) {
+          uint32_t p[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + off);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, v[j]);
+        }
+      }
+    }
+  } else if (warp >= kConvWarp0) {
+    // ------------------------------------------------------------------ converters (both CTAs)
+    const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..255
+    int stage = 0, bstage = 0;
+    uint32_t phase = 0, bphase = 0;
+    bool ok = true;
+    for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+      int m_blk, n_blk;
+      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
+      Dec<kV, kFast> dec_f[2];
+      if constexpr (!kDX) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int gn = n0 + (ct >> 2) + 64 * j;
+          dec_f[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+        }
+      }
+      const int rot = step_rotation(t, args.main_kb);
+      for (int si = 0; si < nsteps && ok; ++si) {
+        const Step st = step_of(si, args.main_kb, rot);
+        if (!mbar_wait(bar(bars->w_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+          ok = false;
+          break;
+        }
+        for (int sub = 0; sub < st.nsub; ++sub) {
+          if (!mbar_wait_cluster(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status,
+                                 MOSS_STATUS_TIMEOUT_CONVERT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t b_base = b_smem + bstage * kBBytes;
+          if constexpr (!kDX) {
+            // forward: K-major B half [128 n][64 k]; thread rows (ct >> 2) + 64 j, chunk ct & 3
+            const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
+            const int c = ct & 3;
+            uint4 o[2][2];
+            if (!st.ext) {
+              uint4 qv[2];
+#pragma unroll
+              for (int j = 0; j < 2; ++j) qv[j] = lds128(w_base + ((ct >> 2) + 64 * j) * 64 + c * 16);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) dec_f[j].chunk(qv[j], args.w_kind, o[j][0], o[j][1]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                float f[16];
+                const int gn = n0 + (ct >> 2) + 64 * j;
+                if (gn < args.Nc) {
+                  load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gn) * args.ld_ext_b,
+                             st.first_kb * BK + c * 16, args.ext_r, f);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+                }
+                pack16_scaled(f, args.ext_scale, kV, o[j][0], o[j][1]);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int row = (ct >> 2) + 64 * j;
+              const uint32_t rbase = b_base + (row >> 3) * 1024 + (row & 7) * 128;
+              sts128(rbase + ((((2 * c) ^ (row & 7)) & 7) << 4), o[j][0]);
+              sts128(rbase + ((((2 * c + 1) ^ (row & 7)) & 7) << 4), o[j][1]);
+            }
+          } else {
+            // grad-input: MN-major B half [64 n][128 k] as two 64-column atoms; the int8
+            // stage holds kSub * 64 reduction rows of 128 bytes (128B swizzle).
+            const int cw = ct >> 5;
+            const int ph = lane >> 3;
+            const int hi = (lane >> 2) & 1;
+            const int qd = lane & 3;
+            const int r_in = hi ? (ph ^ 5) : ph;  // row pairs (0,5) (1,4) (2,7) (3,6)
+            const int row = cw * 8 + r_in;
+            uint4 o[2][2];
+            if (!st.ext) {
+              Dec<kV, kFast> dec;
+              const int gn = (st.first_kb + sub) * BK + row;
+              dec.set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+              const uint32_t w_base = w_smem + stage * kWStage + (sub * BK + row) * 128;
+              uint4 qv[2];
+#pragma unroll
+              for (int a = 0; a < 2; ++a) qv[a] = lds128(w_base + ((((4 * a + qd) ^ r_in) & 7) << 4));
+#pragma unroll
+              for (int a = 0; a < 2; ++a) dec.chunk(qv[a], args.w_kind, o[a][0], o[a][1]);
+            } else {
+#pragma unroll
+              for (int a = 0; a < 2; ++a) {
+                float f[16];
+                const int gj = st.first_kb * BK + row;
+                if (gj < args.ext_r) {
+                  load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gj) * args.ld_ext_b,
+                             n0 + (4 * a + qd) * 16, args.Nc, f);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) f[i] = 0.0f;
+                }
+                pack16_scaled(f, args.ext_scale, kV, o[a][0], o[a][1]);
+              }
+            }
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+              const uint32_t rbase = b_base + a * (kBBytes / 2) + row * 128;
+              sts128(rbase + ((((2 * qd) ^ r_in) & 7) << 4), o[a][0]);
+              sts128(rbase + ((((2 * qd + 1) ^ r_in) & 7) << 4), o[a][1]);
+            }
+          }
+          // b_full also certifies this CTA's A rows: the leader's MMA reads both CTAs' halves.
+          if (sub == 0 &&
+              !mbar_wait(bar(bars->a_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t fb = bar(bars->b_full[bstage]);
+            if (leader)
+              mbar_arrive(fb);
+            else
+              mbar_arrive_cluster(mapa_shared(fb, 0));
+          }
+          if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
+        }
+        if (!ok) break;
+        if (lane == 0) mbar_arrive(bar(bars->empty[stage]));
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  }
+
+  // Leave together: the leader's MMAs read the peer's shared memory and write its TMEM, and
+  // the peer arrives on the leader's barriers, so neither CTA may exit or free TMEM first.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(mapa_shared(bar(bars->exit_bar), rank ^ 1u));
+    const long long start = clock64();
+    while (!mbar_try_wait_cluster(bar(bars->exit_bar), 0)) {
+      if (clock64() - start > kWaitBudgetCycles) {
+        report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+template <bool kDX, int kV, bool kFast>
+static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& te, const Args& a,
+                        cudaStream_t stream) {
+  auto kern = w8_gemm_pair_kernel<kDX, kV, kFast>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int max_pairs = 0;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (attr_err != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = sm_count() / 2;
+    }
+    max_pairs = clusters;
+  });
+  MOSS_CUDA_TRY(attr_err);
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int pairs = std::max(1, std::min(tiles, max_pairs));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MOSS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tw, te, a));
+  return MOSS_OK;
+}
+
+}  // namespace pair
+
+int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t s) {
+  using namespace pair;
+  // A: [M, Kr] viewed as {64, M, Kr / 64} so one box carries kSub k-blocks of 128 rows.
+  if (a.Kr % BK != 0) return MOSS_ERR_UNSUPPORTED;
+  const CUtensorMapDataType v_dt = v_kind == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tw, te;
+  memset(&ta, 0, sizeof(ta));
+  memset(&tw, 0, sizeof(tw));
+  memset(&te, 0, sizeof(te));
+  {
+    const uint64_t dims[3] = {BK, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.Kr / BK)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.lda) * 2, BK * 2};
+    const uint32_t box[3] = {BK, kHalf, kSub};
+    if (!make_map_nd(&ta, v_dt, 2, a.a, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return MOSS_ERR_UNSUPPORTED;
+  }
+  if (!dx) {
+    // weight [N, K] int8 viewed as {64, N, K / 64}: [kSub][128 rows][64 B] per box
+    if (a.w_cols % BK != 0) return MOSS_ERR_UNSUPPORTED;
+    const uint64_t dims[3] = {BK, static_cast<uint64_t>(a.w_rows), static_cast<uint64_t>(a.w_cols / BK)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.ldw), BK};
+    const uint32_t box[3] = {BK, kHalf, kSub};
+    if (!make_map_nd(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return MOSS_ERR_UNSUPPORTED;
+  } else {
+    // weight rows are reduction indices: one box = kSub * 64 rows x 128 output columns
+    if (!make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.w_cols, a.w_rows, a.ldw, 128, BK * kSub,
+                  CU_TENSOR_MAP_SWIZZLE_128B))
+      return MOSS_ERR_UNSUPPORTED;
+  }
+  if (a.ext_r > 0 && !make_map(&te, v_dt, 2, a.ext_a, a.ext_r, a.M, a.ld_ext_a * 2, BK, kHalf,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+    return MOSS_ERR_UNSUPPORTED;
+  if (dx) {
+    if (v_kind == kBF16)
+      return fast ? launch_typed<true, kBF16, true>(ta, tw, te, a, s) : launch_typed<true, kBF16, false>(ta, tw, te, a, s);
+    return fast ? launch_typed<true, kF16, true>(ta, tw, te, a, s) : launch_typed<true, kF16, false>(ta, tw, te, a, s);
+  }
+  if (v_kind == kBF16)
+    return fast ? launch_typed<false, kBF16, true>(ta, tw, te, a, s) : launch_typed<false, kBF16, false>(ta, tw, te, a, s);
+  return fast ? launch_typed<false, kF16, true>(ta, tw, te, a, s) : launch_typed<false, kF16, false>(ta, tw, te, a, s);
+}
+
+}  // namespace gemm
+}  // namespace moss
