@@ -33,8 +33,11 @@ constexpr int kTileN = 256;
 // TMA cost on this part is dominated by a per-operation overhead (about two tensor ops in
 // flight per SM), so each load stage fetches kSub k-blocks with one 3-D box per operand.
 constexpr int kSub = 2;
-constexpr int kStages = 3;
-constexpr int kBStages = 4;
+// Separate rings: an A stage lives until the MMAs that read it retire; an int8 stage only
+// until it is dequantised, so fewer int8 stages are needed.
+constexpr int kAStages = 4;
+constexpr int kWStages = 2;
+constexpr int kBStages = 3;
 constexpr int kConvWarps = 8;
 constexpr int kEpiWarp0 = 4;
 constexpr int kConvWarp0 = 8;
@@ -45,7 +48,7 @@ constexpr uint32_t kAStage = kSub * kABlock;
 constexpr uint32_t kWStage = kSub * kWBlock;
 constexpr uint32_t kBBytes = kHalf * BK * 2;  // 16 KB converted operand per k-block
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
-constexpr uint32_t kDataBytes = kStages * (kAStage + kWStage) + kBStages * kBBytes;
+constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStages * kBBytes;
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
@@ -92,9 +95,10 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap
 }
 
 struct Barriers {
-  uint64_t a_full[kStages];    // local: this CTA's A half landed
-  uint64_t w_full[kStages];    // local: this CTA's int8 half landed
-  uint64_t empty[kStages];     // local: A + W stage free (MMA commit + local converters)
+  uint64_t a_full[kAStages];   // local: this CTA's A half landed
+  uint64_t a_empty[kAStages];  // local: A stage free (MMA commit)
+  uint64_t w_full[kWStages];   // local: this CTA's int8 half landed
+  uint64_t w_empty[kWStages];  // local: int8 stage free (local converters)
   uint64_t b_full[kBStages];   // leader: both CTAs' converted halves written
   uint64_t b_empty[kBStages];  // local: converted stage free (MMA commit)
   uint64_t acc_full[2];        // local: accumulator ready (MMA commit)
@@ -115,8 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* const base_ptr = smem_raw + (base - raw_base);
   const uint32_t a_smem = base;
-  const uint32_t w_smem = base + kStages * kAStage;
-  const uint32_t b_smem = w_smem + kStages * kWStage;
+  const uint32_t w_smem = base + kAStages * kAStage;
+  const uint32_t b_smem = w_smem + kWStages * kWStage;
   Barriers* bars = reinterpret_cast<Barriers*>(base_ptr + kDataBytes);
   auto bar = [&](uint64_t& b) { return smem_u32(&b); };
   volatile int* abort_flag = &bars->abort_flag;
@@ -131,10 +135,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nsteps = steps_per_tile(args);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kAStages; ++s) {
       mbar_init(bar(bars->a_full[s]), 1);
+      mbar_init(bar(bars->a_empty[s]), 1);
+    }
+    for (int s = 0; s < kWStages; ++s) {
       mbar_init(bar(bars->w_full[s]), 1);
-      mbar_init(bar(bars->empty[s]), 1 + kConvWarps);
+      mbar_init(bar(bars->w_empty[s]), kConvWarps);
     }
     for (int s = 0; s < kBStages; ++s) {
       mbar_init(bar(bars->b_full[s]), 2 * kConvWarps);
@@ -159,13 +166,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer (both CTAs)
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------ producers (both CTAs)
+    // warp 0 streams the A ring, warp 2 the int8 ring; each waits only on its own ring.
+    const bool a_role = warp == 0;
     if (lane == 0) {
-      tma_prefetch_desc(&tm_a);
-      tma_prefetch_desc(&tm_w);
-      if (args.ext_r > 0) tma_prefetch_desc(&tm_ext);
+      if (a_role) {
+        tma_prefetch_desc(&tm_a);
+        if (args.ext_r > 0) tma_prefetch_desc(&tm_ext);
+      } else {
+        tma_prefetch_desc(&tm_w);
+      }
     }
+    const int nst = a_role ? kAStages : kWStages;
     int stage = 0;
     uint32_t phase = 0;
     uint32_t used_mask = 0, last_phase_mask = 0;
@@ -178,45 +191,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int rot = step_rotation(t, args.main_kb);
       for (int si = 0; si < nsteps; ++si) {
         const Step st = step_of(si, args.main_kb, rot);
-        if (!mbar_wait_cluster(bar(bars->empty[stage]), phase ^ 1u, abort_flag, args.status,
-                               MOSS_STATUS_TIMEOUT_LOAD)) {
+        const uint32_t empty_bar = a_role ? bar(bars->a_empty[stage]) : bar(bars->w_empty[stage]);
+        if (!mbar_wait_cluster(empty_bar, phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          const uint32_t a_dst = a_smem + stage * kAStage;
-          const uint32_t w_dst = w_smem + stage * kWStage;
-          const uint32_t a_bar = bar(bars->a_full[stage]);
-          const uint32_t w_bar = bar(bars->w_full[stage]);
-          if (!st.ext) {
-            // one op per operand for kSub k-blocks (chunks past K are zero-filled)
-            mbar_arrive_expect_tx(a_bar, kAStage);
-            tma_load_3d(a_dst, &tm_a, a_bar, 0, m0, st.first_kb);
-            mbar_arrive_expect_tx(w_bar, kWStage);
-            if constexpr (!kDX) {
-              tma_load_3d(w_dst, &tm_w, w_bar, 0, n0, st.first_kb);
+          if (a_role) {
+            const uint32_t a_dst = a_smem + stage * kAStage;
+            const uint32_t a_bar = bar(bars->a_full[stage]);
+            if (!st.ext) {
+              // one op for kSub k-blocks (chunks past K are zero-filled)
+              mbar_arrive_expect_tx(a_bar, kAStage);
+              tma_load_3d(a_dst, &tm_a, a_bar, 0, m0, st.first_kb);
             } else {
-              tma_load_2d(w_dst, &tm_w, w_bar, n0, st.first_kb * BK);
+              mbar_arrive_expect_tx(a_bar, kABlock);
+              tma_load_2d(a_dst, &tm_ext, a_bar, st.first_kb * BK, m0);
             }
           } else {
-            mbar_arrive_expect_tx(a_bar, kABlock);
-            tma_load_2d(a_dst, &tm_ext, a_bar, st.first_kb * BK, m0);
-            mbar_arrive(w_bar);  // LoRA block: no int8 data, keep the phase
+            const uint32_t w_dst = w_smem + stage * kWStage;
+            const uint32_t w_bar = bar(bars->w_full[stage]);
+            if (!st.ext) {
+              mbar_arrive_expect_tx(w_bar, kWStage);
+              if constexpr (!kDX) {
+                tma_load_3d(w_dst, &tm_w, w_bar, 0, n0, st.first_kb);
+              } else {
+                tma_load_2d(w_dst, &tm_w, w_bar, n0, st.first_kb * BK);
+              }
+            } else {
+              mbar_arrive(w_bar);  // LoRA block: no int8 data, keep the phase
+            }
           }
           used_mask |= 1u << stage;
           last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
         }
         __syncwarp();
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++stage == nst) { stage = 0; phase ^= 1u; }
       }
     }
     // Drain our own copies before leaving.
     if (lane == 0) {
-      for (int s = 0; s < kStages; ++s) {
-        if (!((used_mask >> s) & 1u)) continue;
-        const uint32_t ph = (last_phase_mask >> s) & 1u;
+      for (int s2 = 0; s2 < nst; ++s2) {
+        if (!((used_mask >> s2) & 1u)) continue;
+        const uint32_t ph = (last_phase_mask >> s2) & 1u;
+        const uint32_t fb = a_role ? bar(bars->a_full[s2]) : bar(bars->w_full[s2]);
         const long long start = clock64();
-        while (!mbar_try_wait(bar(bars->w_full[s]), ph) || !mbar_try_wait(bar(bars->a_full[s]), ph)) {
+        while (!mbar_try_wait(fb, ph)) {
           if (clock64() - start > kWaitBudgetCycles) {
             report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
             break;
@@ -280,9 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
           }
           if (!ok) break;
-          if (lane == 0) umma_commit_pair_mc(bar(bars->empty[stage]), 0x3);
+          if (lane == 0) umma_commit_pair_mc(bar(bars->a_empty[stage]), 0x3);
           __syncwarp();
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          if (++stage == kAStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         if (lane == 0) umma_commit_pair_mc(bar(bars->acc_full[acc]), 0x3);
@@ -368,8 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters (both CTAs)
     const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..255
-    int stage = 0, bstage = 0;
-    uint32_t phase = 0, bphase = 0;
+    int stage = 0, bstage = 0, astage = 0;
+    uint32_t phase = 0, bphase = 0, aphase = 0;
     bool ok = true;
     for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
       int m_blk, n_blk;
@@ -474,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // b_full also certifies this CTA's A rows: the leader's MMA reads both CTAs' halves.
           if (sub == 0 &&
-              !mbar_wait(bar(bars->a_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+              !mbar_wait(bar(bars->a_full[astage]), aphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
             ok = false;
             break;
           }
@@ -490,8 +510,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
         }
         if (!ok) break;
-        if (lane == 0) mbar_arrive(bar(bars->empty[stage]));
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));
+        if (++stage == kWStages) { stage = 0; phase ^= 1u; }
+        if (++astage == kAStages) { astage = 0; aphase ^= 1u; }
       }
     }
   }
