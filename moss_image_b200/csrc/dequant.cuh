@@ -113,6 +113,13 @@ struct Dec {
       dequant_word_generic(w, s_w, w_kind, kV, lo, hi);
     }
   }
+  // 8 codes -> 16 bytes of 16-bit operand
+  __device__ __forceinline__ uint4 chunk8(uint2 q, int w_kind) const {
+    uint4 o;
+    word(q.x, w_kind, o.x, o.y);
+    word(q.y, w_kind, o.z, o.w);
+    return o;
+  }
   // 16 codes -> 32 bytes of 16-bit operand
   __device__ __forceinline__ void chunk(uint4 q, int w_kind, uint4& o0, uint4& o1) const {
     word(q.x, w_kind, o0.x, o0.y);
@@ -121,6 +128,30 @@ struct Dec {
     word(q.w, w_kind, o1.z, o1.w);
   }
 };
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+// 8 consecutive values of a float-kind row as f32 (zero past `ncols`), times s, packed.
+__device__ __forceinline__ uint4 load8_scaled(const void* base, int kind, int64_t row_off, int col0, int ncols, float s,
+                                              int v_kind) {
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = col0 + i;
+    f[i] = (c < ncols) ? load_as_float(base, kind, row_off + c) * s : 0.0f;
+  }
+  return make_uint4(pack2(f[0], f[1], v_kind), pack2(f[2], f[3], v_kind), pack2(f[4], f[5], v_kind),
+                    pack2(f[6], f[7], v_kind));
+}
+// 256-bit global store (one full 32-byte sector; address 32-byte aligned).
+__device__ __forceinline__ void stg256(void* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),

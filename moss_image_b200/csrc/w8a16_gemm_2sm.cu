@@ -337,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = n_blk * kTileN;
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
-      const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 7) == 0) &&
-                          ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+      const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 15) == 0) &&
+                          ((reinterpret_cast<uintptr_t>(args.out) & 31) == 0);
 #pragma unroll 1
       for (int c = 0; c < kTileN / 32; ++c) {
         uint32_t r[32];
@@ -372,12 +372,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!row_ok) continue;
         const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
         if (vec_ok && col0 + 32 <= args.Nc) {
-          uint32_t p[16];
+          // 64 contiguous bytes per thread as two full 32-byte sectors
+          uint32_t p0[8], p1[8];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + off);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+          for (int j = 0; j < 8; ++j) {
+            p0[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
+            p1[j] = pack2(v[16 + 2 * j], v[16 + 2 * j + 1], args.out_kind);
+          }
+          uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
+          stg256(dst, p0);
+          stg256(dst + 16, p1);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
@@ -395,12 +399,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_blk, n_blk;
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
-      Dec<kV, kFast> dec_f[2];
+      // Conflict-free mapping: the 8 lanes of each quarter-warp cover one 128-byte operand
+      // row; lane (l % 8) converts 8 codes into one 16-byte chunk. Task i of thread ct is
+      // row 4 * warp + lane / 8 + 32 * i (forward), with chunk lane % 8.
+      const int crow = (ct >> 5) * 4 + (lane >> 3);  // 0..31
+      const int cch = lane & 7;
+      Dec<kV, kFast> dec_f[4];
       if constexpr (!kDX) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int gn = n0 + (ct >> 2) + 64 * j;
-          dec_f[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+        for (int i = 0; i < 4; ++i) {
+          const int gn = n0 + crow + 32 * i;
+          dec_f[i].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
         }
       }
       const int rot = step_rotation(t, args.main_kb);
@@ -418,78 +427,65 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t b_base = b_smem + bstage * kBBytes;
           if constexpr (!kDX) {
-            // forward: K-major B half [128 n][64 k]; thread rows (ct >> 2) + 64 j, chunk ct & 3
+            // forward: K-major B half [128 n][64 k], int8 stage rows of 64 bytes
             const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
-            const int c = ct & 3;
-            uint4 o[2][2];
+            uint4 o[4];
             if (!st.ext) {
-              uint4 qv[2];
+              uint2 qv[4];
 #pragma unroll
-              for (int j = 0; j < 2; ++j) qv[j] = lds128(w_base + ((ct >> 2) + 64 * j) * 64 + c * 16);
+              for (int i = 0; i < 4; ++i) qv[i] = lds64(w_base + (crow + 32 * i) * 64 + cch * 8);
 #pragma unroll
-              for (int j = 0; j < 2; ++j) dec_f[j].chunk(qv[j], args.w_kind, o[j][0], o[j][1]);
+              for (int i = 0; i < 4; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
             } else {
 #pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                float f[16];
-                const int gn = n0 + (ct >> 2) + 64 * j;
-                if (gn < args.Nc) {
-                  load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gn) * args.ld_ext_b,
-                             st.first_kb * BK + c * 16, args.ext_r, f);
-                } else {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i) f[i] = 0.0f;
-                }
-                pack16_scaled(f, args.ext_scale, kV, o[j][0], o[j][1]);
+              for (int i = 0; i < 4; ++i) {
+                const int gn = n0 + crow + 32 * i;
+                o[i] = gn < args.Nc ? load8_scaled(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gn) * args.ld_ext_b,
+                                                   st.first_kb * BK + cch * 8, args.ext_r, args.ext_scale, kV)
+                                    : make_uint4(0, 0, 0, 0);
               }
             }
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int row = (ct >> 2) + 64 * j;
-              const uint32_t rbase = b_base + (row >> 3) * 1024 + (row & 7) * 128;
-              sts128(rbase + ((((2 * c) ^ (row & 7)) & 7) << 4), o[j][0]);
-              sts128(rbase + ((((2 * c + 1) ^ (row & 7)) & 7) << 4), o[j][1]);
+            for (int i = 0; i < 4; ++i) {
+              const int row = crow + 32 * i;
+              sts128(b_base + (row >> 3) * 1024 + (row & 7) * 128 + (((cch ^ (row & 7)) & 7) << 4), o[i]);
             }
           } else {
-            // grad-input: MN-major B half [64 n][128 k] as two 64-column atoms; the int8
-            // stage holds kSub * 64 reduction rows of 128 bytes (128B swizzle).
-            const int cw = ct >> 5;
-            const int ph = lane >> 3;
-            const int hi = (lane >> 2) & 1;
-            const int qd = lane & 3;
-            const int r_in = hi ? (ph ^ 5) : ph;  // row pairs (0,5) (1,4) (2,7) (3,6)
-            const int row = cw * 8 + r_in;
-            uint4 o[2][2];
+            // grad-input: MN-major B half = 2 atoms x [64 n][64 k]; the int8 stage holds
+            // kSub * 64 reduction rows of 128 bytes (128B swizzle). Task i: atom i / 2,
+            // reduction row crow + 32 (i % 2), 8 output columns at atom * 64 + cch * 8.
+            uint4 o[4];
             if (!st.ext) {
-              Dec<kV, kFast> dec;
-              const int gn = (st.first_kb + sub) * BK + row;
-              dec.set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-              const uint32_t w_base = w_smem + stage * kWStage + (sub * BK + row) * 128;
-              uint4 qv[2];
+              Dec<kV, kFast> dec[2];
 #pragma unroll
-              for (int a = 0; a < 2; ++a) qv[a] = lds128(w_base + ((((4 * a + qd) ^ r_in) & 7) << 4));
+              for (int h = 0; h < 2; ++h) {
+                const int gn = (st.first_kb + sub) * BK + crow + 32 * h;
+                dec[h].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+              }
+              uint2 qv[4];
 #pragma unroll
-              for (int a = 0; a < 2; ++a) dec.chunk(qv[a], args.w_kind, o[a][0], o[a][1]);
+              for (int i = 0; i < 4; ++i) {
+                const int a = i >> 1, r = crow + 32 * (i & 1);
+                const int q16 = 4 * a + (cch >> 1);
+                qv[i] = lds64(w_smem + stage * kWStage + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) +
+                              (cch & 1) * 8);
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) o[i] = dec[i & 1].chunk8(qv[i], args.w_kind);
             } else {
 #pragma unroll
-              for (int a = 0; a < 2; ++a) {
-                float f[16];
-                const int gj = st.first_kb * BK + row;
-                if (gj < args.ext_r) {
-                  load16_f32(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gj) * args.ld_ext_b,
-                             n0 + (4 * a + qd) * 16, args.Nc, f);
-                } else {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i) f[i] = 0.0f;
-                }
-                pack16_scaled(f, args.ext_scale, kV, o[a][0], o[a][1]);
+              for (int i = 0; i < 4; ++i) {
+                const int a = i >> 1, r = crow + 32 * (i & 1);
+                const int gj = st.first_kb * BK + r;
+                o[i] = gj < args.ext_r ? load8_scaled(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gj) * args.ld_ext_b,
+                                                      n0 + a * 64 + cch * 8, args.Nc, args.ext_scale, kV)
+                                       : make_uint4(0, 0, 0, 0);
               }
             }
 #pragma unroll
-            for (int a = 0; a < 2; ++a) {
-              const uint32_t rbase = b_base + a * (kBBytes / 2) + row * 128;
-              sts128(rbase + ((((2 * qd) ^ r_in) & 7) << 4), o[a][0]);
-              sts128(rbase + ((((2 * qd + 1) ^ r_in) & 7) << 4), o[a][1]);
+            for (int i = 0; i < 4; ++i) {
+              const int a = i >> 1, r = crow + 32 * (i & 1);
+              sts128(b_base + a * (kBBytes / 2) + r * 128 + (((cch ^ (r & 7)) & 7) << 4), o[i]);
             }
           }
           // b_full also certifies this CTA's A rows: the leader's MMA reads both CTAs' halves.
