@@ -80,6 +80,15 @@ MOSS_API int moss_w8_dequantize(const int8_t* q, const float* scale, int64_t n, 
                        void* out, moss_stream_t stream);
 
 /*
+ * Scratch bytes the GEMM entry points use for the given problem (k_red = reduction length,
+ * n_out = output columns), 0 when none. Small-M problems split the reduction across CTAs
+ * (split-K) and exchange f32 partial tiles through this workspace; with a NULL or smaller
+ * workspace they run unsplit (same result, lower occupancy). New in this library: the
+ * reference's Triton launchers take no workspace (training/quant_kernels.py:294-373).
+ */
+MOSS_API int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t k_red, size_t* bytes);
+
+/*
  * Weight-only int8 GEMM, forward:
  *   y[m, n] = round_x( sum_k x[m,k] * dec(q)[n,k]  + round_x(bias[n])
  *                      + lora_scale * sum_j lora_xa[m,j] * round_x(lora_b[n,j]) )
@@ -93,12 +102,13 @@ MOSS_API int moss_w8_dequantize(const int8_t* q, const float* scale, int64_t n, 
  *   lora_xa nullable device [m, lora_rank] in x_dtype (x @ lora_A^T, unscaled)
  *   lora_b  device [n, lora_rank] in lora_b_dtype (required when lora_xa is given)
  *   y       device [m, n] contiguous in y_dtype
+ *   workspace nullable device scratch (256-byte aligned) of moss_w8a16_gemm_workspace_bytes(m, n, k)
  */
 MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* q,
                         const float* scale, int weight_dtype, int64_t n, const void* bias,
                         int bias_dtype, const void* lora_xa, const void* lora_b, int lora_b_dtype,
-                        int64_t lora_rank, float lora_scale, void* y, int y_dtype, int* status,
-                        moss_stream_t stream);
+                        int64_t lora_rank, float lora_scale, void* y, int y_dtype, void* workspace,
+                        size_t workspace_bytes, int* status, moss_stream_t stream);
 
 /*
  * Weight-only int8 GEMM, grad-input (no weight gradient: the base is frozen):
@@ -112,11 +122,13 @@ MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t 
  *   dy       device [m, n] contiguous, dy_dtype F16 or BF16
  *   lora_dyb nullable device [m, lora_rank] in dy_dtype (dy @ lora_B, unscaled)
  *   lora_a   device [lora_rank, k] in lora_a_dtype (required when lora_dyb is given)
+ *   workspace nullable device scratch (256-byte aligned) of moss_w8a16_gemm_workspace_bytes(m, k, n)
  */
 MOSS_API int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
                        const float* scale, int weight_dtype, int64_t k, const void* lora_dyb,
                        const void* lora_a, int lora_a_dtype, int64_t lora_rank, float lora_scale,
-                       void* dx, int dx_dtype, int* status, moss_stream_t stream);
+                       void* dx, int dx_dtype, void* workspace, size_t workspace_bytes, int* status,
+                       moss_stream_t stream);
 
 /*
  * Dense gather of a strided (non-overlapping) view into a contiguous buffer, and the

@@ -39,13 +39,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "moss_last_error": (ctypes.c_char_p, []),
     "moss_w8_quantize": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_w8_dequantize": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp, _vp]),
+    "moss_w8a16_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "moss_w8a16_gemm_fwd": (
         _i32,
-        [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _vp],
+        [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _sz,
+         _vp, _vp],
     ),
     "moss_w8a16_gemm_dx": (
         _i32,
-        [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _vp],
+        [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _sz, _vp, _vp],
     ),
     "moss_strided_gather": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "moss_strided_scatter": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),

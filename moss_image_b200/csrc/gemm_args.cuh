@@ -24,7 +24,27 @@ struct Args {
   const void* ext_b; int ext_b_kind; int64_t ld_ext_b; int ext_r;  // fwd [Nc, r]; dx [r, Nc]
   float ext_scale;
   int* status;
+  // split-K (1-CTA kernel): work units are (tile, split); split s covers weight k-blocks
+  // [s * kb_per_split, (s + 1) * kb_per_split) and the last split also the LoRA blocks.
+  // Partial f32 tiles go to `partial` [splits][M][Nc]; `counters` [tiles] count arrivals.
+  int splits, kb_per_split;
+  float* partial;
+  int* counters;
 };
+
+// k-block schedule of one work unit: iteration i -> weight k-block or LoRA block.
+struct UnitRange {
+  int kb0, main_count, n_iter;
+  __device__ __forceinline__ int kb(int i, int main_kb) const { return i < main_count ? kb0 + i : main_kb + (i - main_count); }
+};
+__device__ __forceinline__ UnitRange unit_range(const Args& a, int split) {
+  UnitRange r;
+  r.kb0 = split * a.kb_per_split;
+  const int kb1 = min(a.main_kb, r.kb0 + a.kb_per_split);
+  r.main_count = max(0, kb1 - r.kb0);
+  r.n_iter = r.main_count + (split == a.splits - 1 ? a.num_kb - a.main_kb : 0);
+  return r;
+}
 
 // ------------------------------------------------------------------ host: TMA descriptors
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

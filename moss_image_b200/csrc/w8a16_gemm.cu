@@ -48,6 +48,8 @@ constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 256;
 // Problems with more rows than this use the CTA-pair kernel (256-row tiles) when TMA can
 // describe them; smaller ones keep 128-row tiles.
 constexpr int64_t kPairMinRows = 128;
+// Split-K (f32 partials through the caller's workspace) is used up to this many rows.
+constexpr int64_t kSplitMaxRows = 32;
 
 struct Barriers {
   uint64_t full[kStages];
@@ -87,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_units = num_tiles * args.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -126,12 +129,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t used_mask = 0;        // stages that received a TMA copy
     uint32_t last_phase_mask = 0;  // phase bit of the last copy per stage
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const int t = u / args.splits;
+      const UnitRange ur = unit_range(args, u - t * args.splits);
       int m_blk, n_blk;
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int m0 = m_blk * BM;
       const int n0 = n_blk * BN;
-      for (int kb = 0; kb < args.num_kb; ++kb) {
+      for (int i = 0; i < ur.n_iter; ++i) {
+        const int kb = ur.kb(i, args.main_kb);
         if (!mbar_wait(bar(bars->empty[stage]), phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
           ok = false;
           break;
@@ -222,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     bool ok = true;
     bool issued_any = false;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
+      const UnitRange ur = unit_range(args, u % args.splits);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(bar(bars->acc_empty[acc]), acc_phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      for (int kb = 0; kb < args.num_kb; ++kb) {
+      for (int i = 0; i < ur.n_iter; ++i) {
         if (!mbar_wait(bar(bars->full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA) ||
             !mbar_wait(bar(bars->b_full[bstage]), bphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
           ok = false;
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               bdesc = umma_desc_sw128(b_base + kk * 2048, 8192, 1024);
             }
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (i | kk) != 0 ? 1u : 0u);
           }
           umma_commit(bar(bars->empty[stage]));
           umma_commit(bar(bars->b_empty[bstage]));
@@ -280,7 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      const int t = u / args.splits;
+      const int split = u - t * args.splits;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_EPILOGUE))
@@ -294,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < args.M;
       const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 7) == 0) &&
                           ((reinterpret_cast<uintptr_t>(args.out) & 15) == 0);
+      const bool split_k = args.splits > 1;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -306,6 +316,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int col0 = n0 + c * 32;
         if (col0 >= args.Nc) continue;
+        if (split_k) {
+          // partial f32 sums of this split; reduced below by the tile's last split
+          if (!row_ok) continue;
+          float* dst = args.partial + (static_cast<int64_t>(split) * args.M + row) * args.Nc + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < args.Nc) dst[j] = __uint_as_float(r[j]);
+          continue;
+        }
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -331,6 +350,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, v[j]);
         }
       }
+      if (!split_k) continue;
+      // Per 32-row slice (one epilogue warp): the last split to finish reduces all partials of
+      // the slice in split order (deterministic). Warps never wait on each other here.
+      __threadfence();
+      __syncwarp();
+      int done = 0;
+      if (lane == 0) done = atomicAdd(args.counters + t * 4 + q, 1);
+      done = __shfl_sync(0xffffffffu, done, 0);
+      if (done != args.splits - 1) continue;
+      __threadfence();
+      if (row_ok) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = n0 + c * 32;
+          if (col0 >= args.Nc) break;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+          for (int sp = 0; sp < args.splits; ++sp) {
+            const float* src = args.partial + (static_cast<int64_t>(sp) * args.M + row) * args.Nc + col0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.Nc) v[j] += __ldcg(src + j);
+          }
+          const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j >= args.Nc) break;
+            float x = v[j];
+            if constexpr (!kDX) {
+              if (args.bias != nullptr) x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+            }
+            store_from_float(args.out, args.out_kind, off + j, round_to_kind(x, kV));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) args.counters[t * 4 + q] = 0;  // ready for the next call
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -338,7 +395,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0, bstage = 0;
     uint32_t phase = 0, bphase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const int t = u / args.splits;
+      const UnitRange ur = unit_range(args, u - t * args.splits);
       int m_blk, n_blk;
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int n0 = n_blk * BN;
@@ -351,7 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           dec_f[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
         }
       }
-      for (int kb = 0; kb < args.num_kb; ++kb) {
+      for (int i = 0; i < ur.n_iter; ++i) {
+        const int kb = ur.kb(i, args.main_kb);
         if (!mbar_wait(bar(bars->full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT) ||
             !mbar_wait(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
           ok = false;
@@ -475,8 +535,8 @@ static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUte
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
   MOSS_CUDA_TRY(attr_err);
-  const int tiles = a.tiles_m * a.tiles_n;
-  const int grid = std::min(tiles, sm_count());
+  const int units = a.tiles_m * a.tiles_n * a.splits;
+  const int grid = std::min(units, sm_count());
   kern<<<grid, kThreads, kSmemBytes, stream>>>(ta, tw, te, a);
   MOSS_CUDA_TRY(cudaGetLastError());
   return MOSS_OK;
@@ -491,12 +551,44 @@ static int dispatch(int v_kind, bool fast, const CUtensorMap& ta, const CUtensor
   return fast ? launch_typed<kDX, kF16, true>(ta, tw, te, a, s) : launch_typed<kDX, kF16, false>(ta, tw, te, a, s);
 }
 
+// Split-K plan of the 1-CTA kernel (small M: too few output tiles to occupy the GPU).
+struct SplitPlan {
+  int splits = 1;
+  int kb_per_split = 0;
+  size_t partial_bytes = 0;
+  size_t counter_bytes = 0;
+  size_t total() const { return splits > 1 ? partial_bytes + counter_bytes : 0; }
+};
+
+static bool use_pair(int64_t M, int64_t Nc, int sms) {
+  if (M <= kPairMinRows) return false;
+  const int64_t pair_tiles = ((M + 255) / 256) * ((Nc + 255) / 256);
+  return pair_tiles * 4 >= sms;  // the pair grid fills at least half of the SMs
+}
+
+static SplitPlan plan_split(int64_t M, int64_t Nc, int64_t Kr, int sms) {
+  SplitPlan p;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((Nc + BN - 1) / BN);
+  const int64_t main_kb = (Kr + BK - 1) / BK;
+  // Only for a few rows: the f32 partials then cost far less than the weight bytes.
+  if (M > kSplitMaxRows || tiles <= 0 || tiles * 2 >= sms || main_kb < 8) return p;
+  int64_t want = std::min<int64_t>((sms + tiles - 1) / tiles, std::min<int64_t>(main_kb / 4, 32));
+  if (want < 2) return p;
+  const int64_t kps = (main_kb + want - 1) / want;
+  p.splits = static_cast<int>((main_kb + kps - 1) / kps);
+  p.kb_per_split = static_cast<int>(kps);
+  if (p.splits < 2) return SplitPlan{};
+  p.partial_bytes = (static_cast<size_t>(p.splits) * M * Nc * 4 + 255) / 256 * 256;
+  p.counter_bytes = (static_cast<size_t>(tiles) * 4 * 4 + 255) / 256 * 256;
+  return p;
+}
+
 // Shared driver for both directions.
 //   A: [M, Kr] in v_kind (x or dy); weight q: [w_rows, w_cols]; C: [M, Nc]
 static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, int64_t Nc, const int8_t* q,
                const float* scale, int w_kind, int64_t w_rows, int64_t w_cols, const void* bias, int bias_kind,
                const void* ext_a, const void* ext_b, int ext_b_kind, int64_t ext_r, float ext_scale, void* out,
-               int out_kind, int* status, cudaStream_t stream) {
+               int out_kind, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
   if (M < 0 || Kr < 0 || Nc < 0) return fail(MOSS_ERR_INVALID_ARGUMENT, "negative GEMM shape");
   if (v_kind != kBF16 && v_kind != kF16)
     return fail(MOSS_ERR_UNSUPPORTED, "compute dtype must be float16 or bfloat16 (got code %d)", v_kind);
@@ -551,6 +643,10 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.ext_r = ext_a ? static_cast<int>(ext_r) : 0;
   a.ext_scale = ext_scale;
   a.status = status;
+  a.splits = 1;
+  a.kb_per_split = a.main_kb;
+  a.partial = nullptr;
+  a.counters = nullptr;
 
   CUtensorMap ta, tw, te;
   memset(&ta, 0, sizeof(ta));
@@ -570,7 +666,8 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
     tma = make_map(&te, v_dt, 2, ext_a, ext_r, M, ext_r * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
-  if (tma && M > kPairMinRows) {
+  const int sms = sm_count();
+  if (tma && use_pair(M, Nc, sms)) {
     // CTA-pair kernel: 256 x 256 tiles, multi-k-block TMA boxes; falls through when the
     // shapes do not fit its boxes.
     Args a2 = a;
@@ -578,6 +675,15 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
     a2.tiles_n = static_cast<int>((Nc + 255) / 256);
     const int rc = launch_pair(dx, v_kind, fast, a2, stream);
     if (rc != MOSS_ERR_UNSUPPORTED) return rc;
+  }
+  const SplitPlan plan = plan_split(M, Nc, Kr, sms);
+  if (plan.splits > 1 && workspace != nullptr && workspace_bytes >= plan.total() &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+    a.splits = plan.splits;
+    a.kb_per_split = plan.kb_per_split;
+    a.partial = static_cast<float*>(workspace);
+    a.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + plan.partial_bytes);
+    MOSS_CUDA_TRY(cudaMemsetAsync(a.counters, 0, plan.counter_bytes, stream));
   }
   return dx ? dispatch<true>(v_kind, fast, ta, tw, te, a, stream) : dispatch<false>(v_kind, fast, ta, tw, te, a, stream);
 }
@@ -587,12 +693,23 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
 
 using namespace moss;
 
+extern "C" int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t k_red, size_t* bytes) {
+  if (bytes == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null bytes pointer");
+  *bytes = 0;
+  if (m <= 0 || n_out <= 0 || k_red <= 0) return clear_ok();
+  const int sms = gemm::sm_count();
+  if (gemm::use_pair(m, n_out, sms)) return clear_ok();
+  *bytes = gemm::plan_split(m, n_out, k_red, sms).total();
+  return clear_ok();
+}
+
 extern "C" int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* q,
                                    const float* scale, int weight_dtype, int64_t n, const void* bias, int bias_dtype,
                                    const void* lora_xa, const void* lora_b, int lora_b_dtype, int64_t lora_rank,
-                                   float lora_scale, void* y, int y_dtype, int* status, moss_stream_t stream) {
+                                   float lora_scale, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                                   int* status, moss_stream_t stream) {
   const int rc = gemm::run(false, x, x_dtype, m, k, n, q, scale, weight_dtype, n, k, bias, bias_dtype, lora_xa, lora_b,
-                           lora_b_dtype, lora_rank, lora_scale, y, y_dtype, status,
+                           lora_b_dtype, lora_rank, lora_scale, y, y_dtype, workspace, workspace_bytes, status,
                            reinterpret_cast<cudaStream_t>(stream));
   return rc == MOSS_OK ? clear_ok() : rc;
 }
@@ -600,9 +717,10 @@ extern "C" int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_
 extern "C" int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
                                   const float* scale, int weight_dtype, int64_t k, const void* lora_dyb,
                                   const void* lora_a, int lora_a_dtype, int64_t lora_rank, float lora_scale, void* dx,
-                                  int dx_dtype, int* status, moss_stream_t stream) {
+                                  int dx_dtype, void* workspace, size_t workspace_bytes, int* status,
+                                  moss_stream_t stream) {
   const int rc = gemm::run(true, dy, dy_dtype, m, n, k, q, scale, weight_dtype, n, k, nullptr, 0, lora_dyb, lora_a,
-                           lora_a_dtype, lora_rank, lora_scale, dx, dx_dtype, status,
+                           lora_a_dtype, lora_rank, lora_scale, dx, dx_dtype, workspace, workspace_bytes, status,
                            reinterpret_cast<cudaStream_t>(stream));
   return rc == MOSS_OK ? clear_ok() : rc;
 }

@@ -13,6 +13,7 @@ without edits. Differences, by design:
 
 from __future__ import annotations
 
+import ctypes
 from typing import Literal
 
 import torch
@@ -139,6 +140,21 @@ def _compute_kind(dtype: torch.dtype) -> int:
     return _lib.DTYPE_CODES[dtype]
 
 
+def _workspace(m: int, n_out: int, k_red: int, device: torch.device) -> tuple[torch.Tensor | None, int | None, int]:
+    """Scratch for split-K small-M launches from torch's caching allocator.
+
+    Returns (owner tensor, 256-byte aligned address, bytes); the caller keeps the owner alive
+    until the launch is enqueued (later reuse is ordered by the stream).
+    """
+    size = ctypes.c_size_t()
+    _lib.check(_lib.library().moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)),
+               "moss_w8a16_gemm_workspace_bytes")
+    if size.value == 0:
+        return None, None, 0
+    buf = torch.empty(size.value + 256, dtype=torch.uint8, device=device)
+    return buf, (buf.data_ptr() + 255) // 256 * 256, size.value
+
+
 def _matrix_view(tokens: torch.Tensor) -> torch.Tensor:
     rows = 1
     for size in tokens.shape[:-1]:
@@ -193,6 +209,8 @@ def int8_linear_forward(
             raise ValueError(f"lora_b must be [{out_features}, {rank}], got {tuple(lora_b.shape)}")
         lora_b = lora_b.contiguous()
     lib = _lib.library()
+    status = status_buffer(tokens.device)  # before the workspace: never carved out of it
+    ws_owner, ws, ws_bytes = _workspace(rows, out_features, in_features, tokens.device)
     done = _launch_observer("fwd", rows, out_features, in_features, tokens.device) if _launch_observer else None
     rc = lib.moss_w8a16_gemm_fwd(
         _lib.ptr(matrix), v_kind, rows, in_features,
@@ -200,11 +218,12 @@ def int8_linear_forward(
         _lib.ptr(bias), _lib.DTYPE_CODES.get(bias.dtype, -1) if bias is not None else 0,
         _lib.ptr(lora_xa), _lib.ptr(lora_b), _lib.DTYPE_CODES.get(lora_b.dtype, -1) if lora_b is not None else 0,
         rank, float(lora_scale),
-        _lib.ptr(output), _lib.DTYPE_CODES[output_dtype],
-        _lib.ptr(status_buffer(tokens.device)), _lib.stream_handle(tokens.device),
+        _lib.ptr(output), _lib.DTYPE_CODES[output_dtype], ws, ws_bytes,
+        _lib.ptr(status), _lib.stream_handle(tokens.device),
     )
     if done is not None:
         done()
+    del ws_owner
     _lib.check(rc, "moss_w8a16_gemm_fwd")
     return output.reshape(*tokens.shape[:-1], out_features)
 
@@ -256,17 +275,20 @@ def int8_linear_backward(
             raise ValueError(f"lora_a must be [{rank}, {in_features}], got {tuple(lora_a.shape)}")
         lora_a = lora_a.contiguous()
     lib = _lib.library()
+    status = status_buffer(gradient.device)
+    ws_owner, ws, ws_bytes = _workspace(rows, in_features, out_features, gradient.device)
     done = _launch_observer("dx", rows, in_features, out_features, gradient.device) if _launch_observer else None
     rc = lib.moss_w8a16_gemm_dx(
         _lib.ptr(matrix), v_kind, rows, out_features,
         _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features,
         _lib.ptr(lora_dyb), _lib.ptr(lora_a), _lib.DTYPE_CODES.get(lora_a.dtype, -1) if lora_a is not None else 0,
         rank, float(lora_scale),
-        _lib.ptr(grad_input), _lib.dtype_code(input_dtype),
-        _lib.ptr(status_buffer(gradient.device)), _lib.stream_handle(gradient.device),
+        _lib.ptr(grad_input), _lib.dtype_code(input_dtype), ws, ws_bytes,
+        _lib.ptr(status), _lib.stream_handle(gradient.device),
     )
     if done is not None:
         done()
+    del ws_owner
     _lib.check(rc, "moss_w8a16_gemm_dx")
     return grad_input.reshape(input_shape)
 

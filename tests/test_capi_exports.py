@@ -48,7 +48,8 @@ def test_version_and_argument_validation_need_no_gpu():
     rc = lib.moss_w8_quantize(None, 7, 4, 4, None, None, None, None)
     assert rc == _lib.MOSS_ERR_UNSUPPORTED
     assert "dtype" in _lib.last_error()
-    rc = lib.moss_w8a16_gemm_fwd(None, 2, 4, 4, None, None, 1, 4, None, 0, None, None, 0, 0, 1.0, None, 1, None, None)
+    rc = lib.moss_w8a16_gemm_fwd(None, 2, 4, 4, None, None, 1, 4, None, 0, None, None, 0, 0, 1.0, None, 1, None, 0,
+                                 None, None)
     assert rc == _lib.MOSS_ERR_UNSUPPORTED  # f32 compute dtype is refused up front
     rc = lib.moss_strided_gather(None, 3, 1, (ctypes.c_int64 * 1)(4), (ctypes.c_int64 * 1)(1), None, None)
     assert rc in (_lib.MOSS_ERR_INVALID_ARGUMENT, _lib.MOSS_ERR_UNSUPPORTED)
@@ -61,7 +62,9 @@ def test_version_and_argument_validation_need_no_gpu():
 def test_empty_problems_are_no_ops_without_device_work():
     lib = _lib.library()
     assert lib.moss_w8a16_gemm_fwd(None, 1, 0, 16, None, None, 1, 8, None, 0, None, None, 0, 0, 1.0, None, 1,
-                                   None, None) == _lib.MOSS_OK
+                                   None, 0, None, None) == _lib.MOSS_OK
     assert lib.moss_w8a16_gemm_dx(None, 1, 0, 8, None, None, 1, 16, None, None, 0, 0, 1.0, None, 1,
-                                  None, None) == _lib.MOSS_OK
+                                  None, 0, None, None) == _lib.MOSS_OK
+    size = ctypes.c_size_t(123)
+    assert lib.moss_w8a16_gemm_workspace_bytes(0, 8, 16, ctypes.byref(size)) == _lib.MOSS_OK and size.value == 0
     assert lib.moss_w8_quantize(None, 1, 0, 16, None, None, None, None) == _lib.MOSS_OK

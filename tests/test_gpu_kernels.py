@@ -7,6 +7,7 @@ plus an elementwise bound of a few bf16 ulps of the output scale.
 
 from __future__ import annotations
 
+import ctypes
 import hashlib
 
 import numpy as np
@@ -238,3 +239,56 @@ def test_full_size_against_fp32_matmul(cuda_device, m, k, n):
     assert O.rel_fro(_np(dx), _np(ref_dx)) <= REL_FRO_TOL
     torch.cuda.synchronize()
     _status_ok(cuda_device)
+
+
+SMALL_M = [
+    (2, 3072, 18432),    # per-block adaLN modulation: batch rows only
+    (16, 3072, 3072),
+    (128, 3072, 3072),
+    (1, 12288, 3072),
+    (64, 1024, 520),     # ragged N
+]
+
+
+@pytest.mark.parametrize("m,k,n", SMALL_M)
+def test_small_m_split_k_forward_and_input_gradient(cuda_device, m, k, n):
+    """Small-M problems split the reduction across CTAs (f32 partials in a workspace,
+    reduced in fixed order by the last split of each tile)."""
+    size = ctypes.c_size_t()
+    _lib.check(_lib.library().moss_w8a16_gemm_workspace_bytes(m, n, k, ctypes.byref(size)), "workspace")
+    assert size.value > 0 or m > 32
+    x, q, s = _rand_problem(m, k, n, seed=m + k + n)
+    bias = torch.randn(n) * 0.5
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    y = qk.int8_linear_forward(x.to(cuda_device, torch.bfloat16), qd, sd, bias.to(cuda_device, torch.bfloat16),
+                               torch.bfloat16, torch.bfloat16)
+    y2 = qk.int8_linear_forward(x.to(cuda_device, torch.bfloat16), qd, sd, bias.to(cuda_device, torch.bfloat16),
+                                torch.bfloat16, torch.bfloat16)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(y, y2), "split-K reduction must be deterministic"
+    expected = O.gemm_fwd(_np(x.to(torch.bfloat16)), q, s, w_kind=O.BF16, v_kind=O.BF16,
+                          bias=_np(bias.to(torch.bfloat16)))
+    _check_close(_np(y), expected, O.BF16)
+    dy = torch.randn(m, n, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+    dx = qk.int8_linear_backward(dy.to(cuda_device), qd, sd, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _check_close(_np(dx), O.gemm_dx(_np(dy), q, s, w_kind=O.BF16, v_kind=O.BF16), O.BF16)
+
+
+def test_split_k_without_workspace_matches(cuda_device):
+    """With no workspace the same problem runs unsplit: same values up to f32 summation order."""
+    m, k, n = 8, 3072, 3072
+    x, q, s = _rand_problem(m, k, n, seed=21)
+    xd = x.to(cuda_device, torch.bfloat16)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    y_split = qk.int8_linear_forward(xd, qd, sd, None, torch.bfloat16, torch.bfloat16)
+    y_plain = torch.empty_like(y_split)
+    rc = _lib.library().moss_w8a16_gemm_fwd(
+        xd.data_ptr(), 1, m, k, qd.data_ptr(), sd.data_ptr(), 1, n, None, 0, None, None, 0, 0, 1.0,
+        y_plain.data_ptr(), 1, None, 0, qk.status_buffer(cuda_device).data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "gemm")
+    torch.cuda.synchronize()
+    assert O.rel_fro(_np(y_split), _np(y_plain)) < 2e-3
