@@ -110,6 +110,38 @@ MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t 
                         int64_t lora_rank, float lora_scale, void* y, int y_dtype, void* workspace,
                         size_t workspace_bytes, int* status, moss_stream_t stream);
 
+/* Size of the split-K scratch array compiled into the library for moss_w8a16_gemm_fwd_noalloc. */
+#define MOSS_W8A16_NOALLOC_SCRATCH_BYTES ((size_t)4 << 20)
+
+/*
+ * The forward GEMM above, for callers that cannot allocate device memory on this path: a
+ * host whose HBM belongs to another allocator (a caching pool that has reserved the free
+ * memory, where a side cudaMalloc fails or makes the pool give memory back), or an FFI
+ * caller (cgo, JNI, ctypes) with no device allocator of its own to pass a workspace from.
+ * Same arguments and result as moss_w8a16_gemm_fwd, minus the workspace: the split-K scratch
+ * is a fixed MOSS_W8A16_NOALLOC_SCRATCH_BYTES array inside the library (one copy on every
+ * device that loads the library, held until the process exits). It calls no cudaMalloc,
+ * cudaFree or other allocating routine; the caller still passes x, q, scale, y and status.
+ *   - The first call on a device, with that device current, looks up the array's device
+ *     address (cudaGetSymbolAddress) and caches it; make that first call before any stream
+ *     capture.
+ *   - Problems whose moss_w8a16_gemm_workspace_bytes(m, n, k) exceeds the array are refused
+ *     with MOSS_ERR_INVALID_ARGUMENT before any launch; use moss_w8a16_gemm_fwd for them.
+ *   - All calls on a device share the one array and it keeps the previous call's contents:
+ *     each call clears the split-K counters on its stream, and the partial tiles are written
+ *     before they are read. Calls whose kernels can overlap on the GPU (different streams
+ *     without an ordering event, or different host threads) race on the array; the caller
+ *     must serialise them.
+ * No counterpart in the reference: its Triton launchers have no scratch and allocate their
+ * outputs through torch.
+ */
+MOSS_API int moss_w8a16_gemm_fwd_noalloc(const void* x, int x_dtype, int64_t m, int64_t k,
+                                const int8_t* q, const float* scale, int weight_dtype, int64_t n,
+                                const void* bias, int bias_dtype, const void* lora_xa,
+                                const void* lora_b, int lora_b_dtype, int64_t lora_rank,
+                                float lora_scale, void* y, int y_dtype, int* status,
+                                moss_stream_t stream);
+
 /*
  * Weight-only int8 GEMM, grad-input (no weight gradient: the base is frozen):
  *   dx[m, k] = round_g( sum_n dy[m,n] * dec(q)[n,k]

@@ -25,6 +25,8 @@ MOSS_ERR_CUDA = 3
 MOSS_ERR_RING_FULL = 4
 MOSS_ERR_NOT_FOUND = 5
 
+NOALLOC_SCRATCH_BYTES = 4 << 20  # MOSS_W8A16_NOALLOC_SCRATCH_BYTES
+
 STATUS_NONFINITE_WEIGHT = 0x1
 STATUS_TIMEOUT_MASK = 0x2 | 0x4 | 0x8 | 0x10 | 0x20
 
@@ -44,6 +46,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _sz,
          _vp, _vp],
+    ),
+    "moss_w8a16_gemm_fwd_noalloc": (
+        _i32,
+        [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i32, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _vp],
     ),
     "moss_w8a16_gemm_dx": (
         _i32,

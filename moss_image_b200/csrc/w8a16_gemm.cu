@@ -724,3 +724,73 @@ extern "C" int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64
                            reinterpret_cast<cudaStream_t>(stream));
   return rc == MOSS_OK ? clear_ok() : rc;
 }
+
+// -----------------------------------------------------------------------------------------
+// Allocation-free forward GEMM (moss_w8a16_gemm_fwd_noalloc).
+//
+// For callers that cannot allocate device memory on this path: a host whose HBM is owned by
+// another allocator (a caching pool that has already reserved the free memory, so a side
+// cudaMalloc fails or makes the pool give memory back), or an FFI caller (cgo, JNI, plain
+// ctypes) that has no device allocator of its own to hand out a workspace. The split-K
+// scratch then lives in one fixed array compiled into this library instead of a caller
+// workspace; nothing here calls cudaMalloc, cudaFree or any allocating routine.
+namespace moss {
+namespace gemm {
+
+constexpr size_t kNoAllocScratchBytes = MOSS_W8A16_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 64;
+
+// One copy per device that loads this library, held until the process exits. In host code
+// this name is only a stand-in for the device symbol, never an address: the device address
+// comes from cudaGetSymbolAddress in noalloc_scratch().
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device, looked up on the first call
+// per device (with that device current) and cached afterwards.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {};
+  int device = -1;
+  MOSS_CUDA_TRY(cudaGetDevice(&device));
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(MOSS_ERR_UNSUPPORTED, "device ordinal %d is beyond the %d devices the static scratch covers", device,
+                kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
+    void* p = nullptr;
+    MOSS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255) != 0)
+      return fail(MOSS_ERR_CUDA, "static split-K scratch has no 256-byte aligned device address");
+    addr[device] = p;
+  }
+  *out = addr[device];
+  return MOSS_OK;
+}
+
+}  // namespace gemm
+}  // namespace moss
+
+extern "C" int moss_w8a16_gemm_fwd_noalloc(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* q,
+                                           const float* scale, int weight_dtype, int64_t n, const void* bias,
+                                           int bias_dtype, const void* lora_xa, const void* lora_b,
+                                           int lora_b_dtype, int64_t lora_rank, float lora_scale, void* y,
+                                           int y_dtype, int* status, moss_stream_t stream) {
+  void* scratch = nullptr;
+  int rc = gemm::noalloc_scratch(&scratch);
+  if (rc != MOSS_OK) return rc;
+  size_t need = 0;
+  rc = moss_w8a16_gemm_workspace_bytes(m, n, k, &need);
+  if (rc != MOSS_OK) return rc;
+  if (need > gemm::kNoAllocScratchBytes)
+    return fail(MOSS_ERR_INVALID_ARGUMENT,
+                "moss_w8a16_gemm_fwd_noalloc: m=%lld n=%lld k=%lld needs %zu bytes of split-K scratch, more than "
+                "the %zu-byte static array; call moss_w8a16_gemm_fwd with a workspace instead",
+                static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k), need,
+                gemm::kNoAllocScratchBytes);
+  // The split-K counters are cleared on the stream inside run() before the kernel; the f32
+  // partials are always written before they are read, so stale contents are harmless.
+  rc = gemm::run(false, x, x_dtype, m, k, n, q, scale, weight_dtype, n, k, bias, bias_dtype, lora_xa, lora_b,
+                 lora_b_dtype, lora_rank, lora_scale, y, y_dtype, scratch, need, status,
+                 reinterpret_cast<cudaStream_t>(stream));
+  return rc == MOSS_OK ? clear_ok() : rc;
+}
