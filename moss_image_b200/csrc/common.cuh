@@ -190,18 +190,23 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Wait on a local barrier that also receives arrivals from the peer CTA (remote arrives, or
+// multicast tcgen05.commit). Default (.acquire.cta) semantics, as with the arrive above: the
+// explicit .acquire.cluster form costs hundreds of nanoseconds per poll on this part. The
+// arrivals it pairs with are issued only after the peer's writes (fenced to the async proxy)
+// or the tensor core's reads are complete.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
       : "r"(bar), "r"(parity), "r"(kTryWaitSuspendNs)
       : "memory");
   return ok != 0;
 }
-// Bounded cluster-scope wait (barriers that receive arrivals from the peer CTA).
+// Bounded wait on a barrier that receives arrivals from the peer CTA.
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                   int* status, int code) {
   if (mbar_try_wait_cluster(bar, parity)) return true;

@@ -11,8 +11,8 @@
 //     B columns held by each CTA at the same shared-memory offsets, and each CTA's TMEM holds
 //     its 128 accumulator rows; completion is committed to both CTAs (multicast commit);
 //   * each CTA's epilogue warps drain their own TMEM half and release it to the leader.
-// Compared with the 1-CTA kernel this halves the dequant work per SM, lowers the operand
-// bytes per FLOP (each SM loads half of the int8 tile), and leaves room for 6 load stages.
+// Compared with the 1-CTA kernel this halves the dequant work per SM and lowers the operand
+// bytes per FLOP (each SM loads half of the int8 tile).
 // The decode rounding is identical (dequant.cuh).
 #include <algorithm>
 #include <mutex>
@@ -34,11 +34,17 @@ constexpr int kTileN = 256;
 // flight per SM), so each load stage fetches kSub k-blocks with one 3-D box per operand.
 constexpr int kSub = 2;
 // Separate rings: an A stage lives until the MMAs that read it retire; an int8 stage only
-// until it is dequantised, so fewer int8 stages are needed.
-constexpr int kAStages = 4;
+// until it is dequantised, so fewer int8 stages are needed. The converted ring is the deepest:
+// two converter groups fill it two k-blocks at a time.
+constexpr int kAStages = 3;
 constexpr int kWStages = 2;
-constexpr int kBStages = 3;
+constexpr int kBStages = 5;
 constexpr int kConvWarps = 8;
+// The converter warps form kSub groups; group g dequantises k-block g of every weight stage,
+// so kSub k-blocks are converted concurrently. A single group working through the k-blocks
+// one at a time is bound by the latency of its per-block chain (shared loads, decode, stores,
+// proxy fence, remote arrive), not by issue bandwidth.
+constexpr int kGroupWarps = kConvWarps / kSub;
 constexpr int kEpiWarp0 = 4;
 constexpr int kConvWarp0 = 8;
 constexpr int kThreads = 16 * 32;
@@ -99,7 +105,7 @@ struct Barriers {
   uint64_t a_empty[kAStages];  // local: A stage free (MMA commit)
   uint64_t w_full[kWStages];   // local: this CTA's int8 half landed
   uint64_t w_empty[kWStages];  // local: int8 stage free (local converters)
-  uint64_t b_full[kBStages];   // leader: both CTAs' converted halves written
+  uint64_t b_full[kBStages];   // leader: both CTAs' converted halves written (one group each)
   uint64_t b_empty[kBStages];  // local: converted stage free (MMA commit)
   uint64_t acc_full[2];        // local: accumulator ready (MMA commit)
   uint64_t acc_empty[2];       // leader: both CTAs drained the accumulator
@@ -144,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(bars->w_empty[s]), kConvWarps);
     }
     for (int s = 0; s < kBStages; ++s) {
-      mbar_init(bar(bars->b_full[s]), 2 * kConvWarps);
+      mbar_init(bar(bars->b_full[s]), 2 * kGroupWarps);
       mbar_init(bar(bars->b_empty[s]), 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -391,7 +397,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters (both CTAs)
-    const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..255
+    const int group = (warp - kConvWarp0) / kGroupWarps;  // the k-block of each stage it converts
+    const int gw = (warp - kConvWarp0) % kGroupWarps;
+    // Conflict-free mapping: the 8 lanes of each quarter-warp cover one 128-byte operand row;
+    // lane (l % 8) converts 8 codes into one 16-byte chunk. Forward task i of a thread is
+    // weight row crow + 16 i; grad-input task i is reduction row crow + 16 (i % 4) of atom i / 4.
+    const int crow = gw * 4 + (lane >> 3);  // 0..15
+    const int cch = lane & 7;
     int stage = 0, bstage = 0, astage = 0;
     uint32_t phase = 0, bphase = 0, aphase = 0;
     bool ok = true;
@@ -399,16 +411,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_blk, n_blk;
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
-      // Conflict-free mapping: the 8 lanes of each quarter-warp cover one 128-byte operand
-      // row; lane (l % 8) converts 8 codes into one 16-byte chunk. Task i of thread ct is
-      // row 4 * warp + lane / 8 + 32 * i (forward), with chunk lane % 8.
-      const int crow = (ct >> 5) * 4 + (lane >> 3);  // 0..31
-      const int cch = lane & 7;
-      Dec<kV, kFast> dec_f[4];
+      Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int gn = n0 + crow + 32 * i;
+        for (int i = 0; i < 8; ++i) {
+          const int gn = n0 + crow + 16 * i;
           dec_f[i].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
         }
       }
@@ -420,89 +427,93 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         for (int sub = 0; sub < st.nsub; ++sub) {
-          if (!mbar_wait_cluster(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status,
-                                 MOSS_STATUS_TIMEOUT_CONVERT)) {
-            ok = false;
-            break;
-          }
-          const uint32_t b_base = b_smem + bstage * kBBytes;
-          if constexpr (!kDX) {
-            // forward: K-major B half [128 n][64 k], int8 stage rows of 64 bytes
-            const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
-            uint4 o[4];
-            if (!st.ext) {
-              uint2 qv[4];
+          if (sub == group) {
+            if (!mbar_wait_cluster(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status,
+                                   MOSS_STATUS_TIMEOUT_CONVERT)) {
+              ok = false;
+              break;
+            }
+            const uint32_t b_base = b_smem + bstage * kBBytes;
+            uint4 o[8];
+            if constexpr (!kDX) {
+              // forward: K-major B half [128 n][64 k], int8 stage rows of 64 bytes
+              const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
+              if (!st.ext) {
+                uint2 qv[8];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) qv[i] = lds64(w_base + (crow + 32 * i) * 64 + cch * 8);
+                for (int i = 0; i < 8; ++i) qv[i] = lds64(w_base + (crow + 16 * i) * 64 + cch * 8);
 #pragma unroll
-              for (int i = 0; i < 4; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
+                for (int i = 0; i < 8; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int gn = n0 + crow + 16 * i;
+                  o[i] = gn < args.Nc ? load8_scaled(args.ext_b, args.ext_b_kind,
+                                                     static_cast<int64_t>(gn) * args.ld_ext_b, st.first_kb * BK + cch * 8,
+                                                     args.ext_r, args.ext_scale, kV)
+                                      : make_uint4(0, 0, 0, 0);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int row = crow + 16 * i;
+                sts128(b_base + (row >> 3) * 1024 + (row & 7) * 128 + (((cch ^ (row & 7)) & 7) << 4), o[i]);
+              }
             } else {
+              // grad-input: MN-major B half = 2 atoms x [64 n][64 k]; the int8 stage holds
+              // kSub * 64 reduction rows of 128 bytes (128B swizzle).
+              if (!st.ext) {
+                Dec<kV, kFast> dec[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int gn = n0 + crow + 32 * i;
-                o[i] = gn < args.Nc ? load8_scaled(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gn) * args.ld_ext_b,
-                                                   st.first_kb * BK + cch * 8, args.ext_r, args.ext_scale, kV)
-                                    : make_uint4(0, 0, 0, 0);
+                for (int j = 0; j < 4; ++j) {
+                  const int gn = (st.first_kb + sub) * BK + crow + 16 * j;
+                  dec[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
+                }
+                uint2 qv[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int a = i >> 2, r = crow + 16 * (i & 3);
+                  const int q16 = 4 * a + (cch >> 1);
+                  qv[i] = lds64(w_smem + stage * kWStage + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) +
+                                (cch & 1) * 8);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = dec[i & 3].chunk8(qv[i], args.w_kind);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int a = i >> 2, r = crow + 16 * (i & 3);
+                  const int gj = st.first_kb * BK + r;
+                  o[i] = gj < args.ext_r ? load8_scaled(args.ext_b, args.ext_b_kind,
+                                                        static_cast<int64_t>(gj) * args.ld_ext_b, n0 + a * 64 + cch * 8,
+                                                        args.Nc, args.ext_scale, kV)
+                                         : make_uint4(0, 0, 0, 0);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int a = i >> 2, r = crow + 16 * (i & 3);
+                sts128(b_base + a * (kBBytes / 2) + r * 128 + (((cch ^ (r & 7)) & 7) << 4), o[i]);
               }
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int row = crow + 32 * i;
-              sts128(b_base + (row >> 3) * 1024 + (row & 7) * 128 + (((cch ^ (row & 7)) & 7) << 4), o[i]);
+            // b_full of a stage's first k-block also certifies this CTA's A rows: the leader's
+            // MMA reads both CTAs' halves, and it issues the stage's k-blocks in order.
+            if (sub == 0 &&
+                !mbar_wait(bar(bars->a_full[astage]), aphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+              ok = false;
+              break;
             }
-          } else {
-            // grad-input: MN-major B half = 2 atoms x [64 n][64 k]; the int8 stage holds
-            // kSub * 64 reduction rows of 128 bytes (128B swizzle). Task i: atom i / 2,
-            // reduction row crow + 32 (i % 2), 8 output columns at atom * 64 + cch * 8.
-            uint4 o[4];
-            if (!st.ext) {
-              Dec<kV, kFast> dec[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int gn = (st.first_kb + sub) * BK + crow + 32 * h;
-                dec[h].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-              }
-              uint2 qv[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int a = i >> 1, r = crow + 32 * (i & 1);
-                const int q16 = 4 * a + (cch >> 1);
-                qv[i] = lds64(w_smem + stage * kWStage + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) +
-                              (cch & 1) * 8);
-              }
-#pragma unroll
-              for (int i = 0; i < 4; ++i) o[i] = dec[i & 1].chunk8(qv[i], args.w_kind);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int a = i >> 1, r = crow + 32 * (i & 1);
-                const int gj = st.first_kb * BK + r;
-                o[i] = gj < args.ext_r ? load8_scaled(args.ext_b, args.ext_b_kind, static_cast<int64_t>(gj) * args.ld_ext_b,
-                                                      n0 + a * 64 + cch * 8, args.Nc, args.ext_scale, kV)
-                                       : make_uint4(0, 0, 0, 0);
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int a = i >> 1, r = crow + 32 * (i & 1);
-              sts128(b_base + a * (kBBytes / 2) + r * 128 + (((cch ^ (r & 7)) & 7) << 4), o[i]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const uint32_t fb = bar(bars->b_full[bstage]);
+              if (leader)
+                mbar_arrive(fb);
+              else
+                mbar_arrive_cluster(mapa_shared(fb, 0));
             }
           }
-          // b_full also certifies this CTA's A rows: the leader's MMA reads both CTAs' halves.
-          if (sub == 0 &&
-              !mbar_wait(bar(bars->a_full[astage]), aphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
-            ok = false;
-            break;
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            const uint32_t fb = bar(bars->b_full[bstage]);
-            if (leader)
-              mbar_arrive(fb);
-            else
-              mbar_arrive_cluster(mapa_shared(fb, 0));
-          }
+          // every group walks every converted stage, so the ring positions stay in step
           if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
         }
         if (!ok) break;
