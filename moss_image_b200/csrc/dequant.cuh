@@ -53,6 +53,50 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int v_kind) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Two f32 values -> one packed pair of the 16-bit compute kind, each rounded to nearest even
+// by a single packed conversion. (A scalar round-trip through the 16-bit type per element is
+// several times more expensive in the epilogue and rounds identically.)
+template <int kV>
+__device__ __forceinline__ uint32_t pack2_kind(float a, float b) {
+  if constexpr (kV == kBF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// Bias of 32 consecutive output columns as f32 values rounded to the compute kind (the
+// reference adds round_v(bias) to the f32 accumulator, training/quant_kernels.py:160-163).
+// A 16-bit bias of the compute kind is exact in f32 and is read as packed words.
+template <int kV>
+__device__ __forceinline__ void load_bias32(const void* bias, int bias_kind, int col0, int ncols, float (&b)[32]) {
+  const uint16_t* b16 = static_cast<const uint16_t*>(bias) + col0;
+  if (bias_kind == kV && col0 + 32 <= ncols && (reinterpret_cast<uintptr_t>(b16) & 15) == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(b16) + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if constexpr (kV == kBF16) {
+          b[8 * i + 2 * k] = __uint_as_float(w[k] << 16);
+          b[8 * i + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+          b[8 * i + 2 * k] = f.x;
+          b[8 * i + 2 * k + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      b[j] = col0 + j < ncols ? round_to_kind(load_as_float(bias, bias_kind, col0 + j), kV) : 0.0f;
+  }
+}
+
 // 16 f32 values times s -> two 16-byte chunks of the 16-bit operand (LoRA factor blocks).
 __device__ __forceinline__ void pack16_scaled(const float (&f)[16], float s, int v_kind, uint4& o0, uint4& o1) {
   o0 = make_uint4(pack2(f[0] * s, f[1] * s, v_kind), pack2(f[2] * s, f[3] * s, v_kind),

@@ -325,29 +325,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (col0 + j < args.Nc) dst[j] = __uint_as_float(r[j]);
           continue;
         }
+        if (!row_ok) continue;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(r[j]);
-          if constexpr (!kDX) {
-            if (args.bias != nullptr && col0 + j < args.Nc)
-              x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if constexpr (!kDX) {
+          if (args.bias != nullptr) {
+            float b[32];
+            load_bias32<kV>(args.bias, args.bias_kind, col0, args.Nc, b);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += b[j];
           }
-          v[j] = round_to_kind(x, kV);
         }
-        if (!row_ok) continue;
         const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
-        if (vec_ok && col0 + 32 <= args.Nc) {
+        if (args.out_kind == kV && vec_ok && col0 + 32 <= args.Nc) {
           uint32_t p[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) p[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
+          for (int j = 0; j < 16; ++j) p[j] = pack2_kind<kV>(v[2 * j], v[2 * j + 1]);
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + off);
 #pragma unroll
           for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, v[j]);
+            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
         }
       }
       if (!split_k) continue;
@@ -375,14 +376,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (col0 + j < args.Nc) v[j] += __ldcg(src + j);
           }
           const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
+          if constexpr (!kDX) {
+            if (args.bias != nullptr) {
+              float b[32];
+              load_bias32<kV>(args.bias, args.bias_kind, col0, args.Nc, b);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j >= args.Nc) break;
-            float x = v[j];
-            if constexpr (!kDX) {
-              if (args.bias != nullptr) x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+              for (int j = 0; j < 32; ++j) v[j] += b[j];
             }
-            store_from_float(args.out, args.out_kind, off + j, round_to_kind(x, kV));
+          }
+          if (args.out_kind == kV && vec_ok && col0 + 32 <= args.Nc) {
+            uint32_t p[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) p[j] = pack2_kind<kV>(v[2 * j], v[2 * j + 1]);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + off);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
           }
         }
       }

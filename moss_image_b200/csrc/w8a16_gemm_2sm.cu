@@ -36,9 +36,9 @@ constexpr int kSub = 2;
 // Separate rings: an A stage lives until the MMAs that read it retire; an int8 stage only
 // until it is dequantised, so fewer int8 stages are needed. The converted ring is the deepest:
 // two converter groups fill it two k-blocks at a time.
-constexpr int kAStages = 3;
-constexpr int kWStages = 2;
-constexpr int kBStages = 5;
+constexpr int kAStages = 4;
+constexpr int kWStages = 3;
+constexpr int kBStages = 3;
 constexpr int kConvWarps = 8;
 // The converter warps form kSub groups; group g dequantises k-block g of every weight stage,
 // so kSub k-blocks are converted concurrently. A single group working through the k-blocks
@@ -58,23 +58,19 @@ constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStag
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
-// LoRA k-block. Every role walks the same sequence.
+// LoRA k-block. Every role walks the same sequence. Tiles in flight at the same time walk K
+// in the same order, so the A rows and weight columns they share are read from L2 while hot.
 struct Step {
   bool ext;
   int first_kb;  // weight k-block (main) or LoRA block index (ext)
   int nsub;
 };
-// `rot` rotates the order of the main steps of a tile: tiles in flight at the same time that
-// share A rows or weight columns then read different k-slices, so they do not all request
-// the same lines at once (the accumulation order differs per tile, not the result set).
-__device__ __forceinline__ Step step_of(int s, int main_kb, int rot) {
+__device__ __forceinline__ Step step_of(int s, int main_kb) {
   const int main_steps = (main_kb + kSub - 1) / kSub;
   Step st;
   if (s < main_steps) {
-    int r = s + rot;
-    if (r >= main_steps) r -= main_steps;
     st.ext = false;
-    st.first_kb = r * kSub;
+    st.first_kb = s * kSub;
     st.nsub = min(kSub, main_kb - st.first_kb);
   } else {
     st.ext = true;
@@ -82,10 +78,6 @@ __device__ __forceinline__ Step step_of(int s, int main_kb, int rot) {
     st.nsub = 1;
   }
   return st;
-}
-__device__ __forceinline__ int step_rotation(int t, int main_kb) {
-  const int main_steps = (main_kb + kSub - 1) / kSub;
-  return main_steps > 0 ? (t * 7) % main_steps : 0;
 }
 __device__ __forceinline__ int steps_per_tile(const Args& a) {
   return (a.main_kb + kSub - 1) / kSub + (a.num_kb - a.main_kb);
@@ -194,9 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
-      const int rot = step_rotation(t, args.main_kb);
       for (int si = 0; si < nsteps; ++si) {
-        const Step st = step_of(si, args.main_kb, rot);
+        const Step st = step_of(si, args.main_kb);
         const uint32_t empty_bar = a_role ? bar(bars->a_empty[stage]) : bar(bars->w_empty[stage]);
         if (!mbar_wait_cluster(empty_bar, phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
           ok = false;
@@ -270,9 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
         bool first = true;
-        const int rot = step_rotation(t, args.main_kb);
-        for (int si = 0; si < nsteps && ok; ++si) {
-          const Step st = step_of(si, args.main_kb, rot);
+          for (int si = 0; si < nsteps && ok; ++si) {
+          const Step st = step_of(si, args.main_kb);
           if (!mbar_wait_cluster(bar(bars->a_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
             ok = false;
             break;
@@ -364,26 +354,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const int col0 = n0 + c * 32;
-        if (col0 >= args.Nc) continue;
+        if (col0 >= args.Nc || !row_ok) continue;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(r[j]);
-          if constexpr (!kDX) {
-            if (args.bias != nullptr && col0 + j < args.Nc)
-              x += round_to_kind(load_as_float(args.bias, args.bias_kind, col0 + j), kV);
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if constexpr (!kDX) {
+          if (args.bias != nullptr) {
+            float b[32];
+            load_bias32<kV>(args.bias, args.bias_kind, col0, args.Nc, b);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += b[j];
           }
-          v[j] = round_to_kind(x, kV);
         }
-        if (!row_ok) continue;
         const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
-        if (vec_ok && col0 + 32 <= args.Nc) {
+        if (args.out_kind == kV && vec_ok && col0 + 32 <= args.Nc) {
           // 64 contiguous bytes per thread as two full 32-byte sectors
           uint32_t p0[8], p1[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            p0[j] = pack2(v[2 * j], v[2 * j + 1], args.out_kind);
-            p1[j] = pack2(v[16 + 2 * j], v[16 + 2 * j + 1], args.out_kind);
+            p0[j] = pack2_kind<kV>(v[2 * j], v[2 * j + 1]);
+            p1[j] = pack2_kind<kV>(v[16 + 2 * j], v[16 + 2 * j + 1]);
           }
           uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
           stg256(dst, p0);
@@ -391,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, v[j]);
+            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
         }
       }
     }
@@ -419,9 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           dec_f[i].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
         }
       }
-      const int rot = step_rotation(t, args.main_kb);
       for (int si = 0; si < nsteps && ok; ++si) {
-        const Step st = step_of(si, args.main_kb, rot);
+        const Step st = step_of(si, args.main_kb);
         if (!mbar_wait(bar(bars->w_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
           ok = false;
           break;
