@@ -135,6 +135,15 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 16 consecutive f32 columns: thread i of the warp gets row (lane base + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 // 32 lanes x 32 consecutive f32 columns: thread i of the warp gets row (lane base + i).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -171,6 +180,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t fmt, bool b_mn_ma
          | ((b_mn_major ? 1u : 0u) << 16)            // B major-ness (A stays K-major)
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+// Same with an explicit A major-ness (A MN-major: a transposed operand in shared memory).
+__host__ __device__ constexpr uint32_t umma_idesc_f16_ab(uint32_t fmt, bool a_mn_major, bool b_mn_major, int m, int n) {
+  return umma_idesc_f16(fmt, b_mn_major, m, n) | ((a_mn_major ? 1u : 0u) << 15);
 }
 
 // ---------------------------------------------------------------- clusters and 2-SM (cta_group::2)

@@ -679,6 +679,24 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
   const int sms = sm_count();
+  if (tma && ext_a == nullptr && M <= kSkinnyMaxRows) {
+    // Few rows: operand-swapped kernel that streams the weight over all SMs.
+    const SkinnyPlan sp = plan_skinny(M, Nc, Kr, sms);
+    if (sp.usable) {
+      Args s = a;
+      s.tiles_n = sp.tiles;
+      if (sp.splits > 1 && workspace != nullptr && workspace_bytes >= sp.total() &&
+          (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+        s.splits = sp.splits;
+        s.kb_per_split = sp.kb_per_split;
+        s.partial = static_cast<float*>(workspace);
+        s.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + sp.partial_bytes);
+        MOSS_CUDA_TRY(cudaMemsetAsync(s.counters, 0, sp.counter_bytes, stream));
+      }
+      const int rc = launch_skinny(dx, v_kind, fast, sp.nt, s, stream);
+      if (rc != MOSS_ERR_UNSUPPORTED) return rc;
+    }
+  }
   if (tma && use_pair(M, Nc, sms)) {
     // CTA-pair kernel: 256 x 256 tiles, multi-k-block TMA boxes; falls through when the
     // shapes do not fit its boxes.
@@ -711,7 +729,12 @@ extern "C" int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t
   if (m <= 0 || n_out <= 0 || k_red <= 0) return clear_ok();
   const int sms = gemm::sm_count();
   if (gemm::use_pair(m, n_out, sms)) return clear_ok();
-  *bytes = gemm::plan_split(m, n_out, k_red, sms).total();
+  // Enough for whichever kernel the call picks: the few-row kernel (no LoRA term) or the
+  // 1-CTA kernel's split-K (with one).
+  size_t need = gemm::plan_split(m, n_out, k_red, sms).total();
+  const gemm::SkinnyPlan sp = gemm::plan_skinny(m, n_out, k_red, sms);
+  if (sp.usable) need = std::max(need, sp.total());
+  *bytes = need;
   return clear_ok();
 }
 

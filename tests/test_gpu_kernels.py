@@ -292,3 +292,55 @@ def test_split_k_without_workspace_matches(cuda_device):
     _lib.check(rc, "gemm")
     torch.cuda.synchronize()
     assert O.rel_fro(_np(y_split), _np(y_plain)) < 2e-3
+
+
+# ------------------------------------------------------------------ few-row (operand-swapped) kernel
+FEW_ROWS = [
+    (1, 3072, 3072),     # one token: 24 feature tiles, split over K
+    (2, 3072, 18432),    # adaLN modulation rows: 144 tiles, no split
+    (16, 12288, 3072),   # MLP down projection, long K split
+    (17, 1024, 1280),    # first row past a 16-token tile
+    (32, 3072, 3072),
+    (33, 2048, 520),     # 64-token tile, ragged features
+    (64, 3072, 1536),
+]
+
+
+@pytest.mark.parametrize("m,k,n", FEW_ROWS)
+@pytest.mark.parametrize("v_dtype", [torch.bfloat16, torch.float16])
+def test_few_row_kernel_forward_and_input_gradient(cuda_device, m, k, n, v_dtype):
+    """At most 64 rows run the operand-swapped kernel (weight as the 128-row MMA operand),
+    split over K when the feature tiles alone cannot occupy the GPU."""
+    v_kind = O.BF16 if v_dtype == torch.bfloat16 else O.F16
+    x, q, s = _rand_problem(m, k, n, seed=1000 + m + n)
+    bias = torch.randn(n, generator=torch.Generator().manual_seed(m)) * 0.5
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    xd = x.to(cuda_device, v_dtype)
+    y = qk.int8_linear_forward(xd, qd, sd, bias.to(cuda_device, v_dtype), v_dtype, v_dtype)
+    y2 = qk.int8_linear_forward(xd, qd, sd, bias.to(cuda_device, v_dtype), v_dtype, v_dtype)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(y, y2), "split-K reduction must be deterministic"
+    expected = O.gemm_fwd(_np(x.to(v_dtype)), q, s, w_kind=v_kind, v_kind=v_kind, bias=_np(bias.to(v_dtype)))
+    _check_close(_np(y), expected, v_kind)
+    dy = torch.randn(m, n, generator=torch.Generator().manual_seed(m + 7)).to(v_dtype)
+    dx = qk.int8_linear_backward(dy.to(cuda_device), qd, sd, torch.Size((m, k)), v_dtype, v_dtype)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _check_close(_np(dx), O.gemm_dx(_np(dy), q, s, w_kind=v_kind, v_kind=v_kind), v_kind)
+
+
+def test_few_row_kernel_mixed_weight_dtype_and_f32_output(cuda_device):
+    """Generic decode (module dtype f32, compute bf16) and an f32 output buffer."""
+    m, k, n = 8, 1024, 640
+    x, q, s = _rand_problem(m, k, n, seed=77)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    xd = x.to(cuda_device, torch.bfloat16)
+    y = torch.empty(m, n, dtype=torch.float32, device=cuda_device)
+    rc = _lib.library().moss_w8a16_gemm_fwd(
+        xd.data_ptr(), 1, m, k, qd.data_ptr(), sd.data_ptr(), 2, n, None, 0, None, None, 0, 0, 1.0,
+        y.data_ptr(), 2, None, 0, qk.status_buffer(cuda_device).data_ptr(), torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "gemm")
+    torch.cuda.synchronize()
+    expected = O.gemm_fwd(_np(x.to(torch.bfloat16)), q, s, w_kind=O.F32, v_kind=O.BF16)
+    _check_close(y.cpu().numpy(), expected, O.BF16)
