@@ -115,16 +115,16 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 // returns MOSS_ERR_UNSUPPORTED (without launching) when the shapes do not fit it.
 int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t stream);
 
-// Few-row kernel (w8a16_gemm_skinny.cu): at most kSkinnyMaxRows activation rows, no LoRA term.
-constexpr int64_t kSkinnyMaxRows = 64;
+// Operand-swapped kernel (w8a16_gemm_skinny.cu): any M without a LoRA term, used when the
+// CTA-pair kernel would leave SMs idle.
 struct SkinnyPlan {
   bool usable = false;
-  int tiles = 0;         // 128-feature tiles
-  int nt = 16;           // token columns of the MMA (16, 32 or 64)
-  int splits = 1;        // K splits (> 1 needs the workspace)
-  int kb_per_split = 0;  // weight k-blocks per split (a multiple of the stage depth)
-  size_t partial_bytes = 0, counter_bytes = 0;
-  size_t total() const { return splits > 1 ? partial_bytes + counter_bytes : 0; }
+  int nt = 16;                   // token tile width = MMA N (16, 32, 64, 128 or 256)
+  int tiles_m = 0, tiles_n = 0;  // token tiles x 128-feature tiles
+  int splits = 1;                // K splits (> 1 needs the workspace for the f32 partials)
+  int kb_per_split = 0;          // weight k-blocks per split (a multiple of the stage depth)
+  size_t partial_bytes = 0;
+  size_t total() const { return splits > 1 ? partial_bytes : 0; }
 };
 SkinnyPlan plan_skinny(int64_t M, int64_t Nc, int64_t Kr, int sms);
 int launch_skinny(bool dx, int v_kind, bool fast, int nt, const Args& a, cudaStream_t stream);

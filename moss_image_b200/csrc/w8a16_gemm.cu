@@ -679,19 +679,20 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
   const int sms = sm_count();
-  if (tma && ext_a == nullptr && M <= kSkinnyMaxRows) {
-    // Few rows: operand-swapped kernel that streams the weight over all SMs.
+  if (tma && ext_a == nullptr && !use_pair(M, Nc, sms)) {
+    // Too few rows for the CTA-pair tiles: operand-swapped kernel that streams the weight over
+    // all SMs (split over K when needed).
     const SkinnyPlan sp = plan_skinny(M, Nc, Kr, sms);
     if (sp.usable) {
       Args s = a;
-      s.tiles_n = sp.tiles;
+      s.tiles_m = sp.tiles_m;
+      s.tiles_n = sp.tiles_n;
       if (sp.splits > 1 && workspace != nullptr && workspace_bytes >= sp.total() &&
           (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
         s.splits = sp.splits;
         s.kb_per_split = sp.kb_per_split;
         s.partial = static_cast<float*>(workspace);
-        s.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + sp.partial_bytes);
-        MOSS_CUDA_TRY(cudaMemsetAsync(s.counters, 0, sp.counter_bytes, stream));
+        s.counters = nullptr;
       }
       const int rc = launch_skinny(dx, v_kind, fast, sp.nt, s, stream);
       if (rc != MOSS_ERR_UNSUPPORTED) return rc;

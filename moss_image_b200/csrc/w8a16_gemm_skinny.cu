@@ -1,5 +1,6 @@
-// Few-row ("skinny") variant of the weight-only int8 GEMM for sm_100a: at most 64 rows of
-// activations (adaLN modulation rows, small batches, decode-like calls).
+// Operand-swapped ("skinny") variant of the weight-only int8 GEMM for sm_100a, used when the
+// activation rows are too few for the CTA-pair kernel to occupy the GPU: adaLN modulation rows,
+// small batches and decode-like calls up to a few thousand rows.
 //
 // With few rows the problem streams the weight: every int8 byte is used M times, so the
 // time is the weight read plus its dequantisation. The 128-row tiles of the other kernels
@@ -9,18 +10,21 @@
 //   grad-input: dX^T[K, M] = dec(W)^T[K, N] * dY^T[N, M]
 // The dequantised weight tile is the 128-row MMA operand A (shared memory; K-major for the
 // forward, MN-major for the grad-input, the same canonical layouts the CTA-pair kernel builds
-// for its B operand) and the activations are a narrow B operand of kNT = 16, 32 or 64
-// columns: tcgen05.mma M = 128, N = kNT. Each accumulator is a kNT-column slice of TMEM whose
-// lane is the output feature.
+// for its B operand) and a tile of kNT = 16 .. 256 activation rows is the B operand:
+// tcgen05.mma M = 128, N = kNT. Each accumulator is a kNT-column slice of TMEM whose lane is the
+// output feature. Per MMA flop it dequantises half as much weight as a 128-row activation tile
+// with 256 features would.
 //
-// Work is split over 128-feature tiles and, when those are too few to occupy the GPU, over K
-// (split-K through the caller's workspace; the last split to finish a 32-feature slice adds
-// the partials in split order, so the result does not depend on timing).
+// Work is split over (token tile, 128-feature tile) pairs and, when those are too few to occupy
+// the GPU, over K: each split writes f32 partials to the caller's workspace and a second, fully
+// parallel kernel adds them in split order (so the result does not depend on timing), adds the
+// bias and rounds. A per-tile "last split reduces" scheme would put up to splits x 256 x 128
+// partials on four warps of one CTA.
 //
 // Warp roles (768 threads, one CTA per SM):
 //   warp 0       TMA producer of the int8 weight stages (kSub k-blocks per box)
 //   warp 1       TMEM owner + single-thread MMA issuer
-//   warp 2       TMA producer of the activation stages (kSub k-blocks per box)
+//   warp 2       TMA producer of the activation stages (kXSub k-blocks per box)
 //   warps 4-7    epilogue, one TMEM lane quarter each
 //   warps 8-23   converters: kGroups groups of 4 warps; group g dequantises k-block g of
 //                every weight stage, so kGroups k-blocks are converted concurrently (one group
@@ -50,27 +54,34 @@ constexpr int kThreads = (kConvWarp0 + kConvWarps) * 32;
 constexpr uint32_t kWBlock = BM * BK;          // 8 KB of int8 per k-block (both directions)
 constexpr uint32_t kWStage = kSub * kWBlock;   // 32 KB
 constexpr uint32_t kCBlock = BM * BK * 2;      // 16 KB converted operand per k-block
-constexpr int kCStages = 5;
+constexpr int kMaxCStages = 5;
 constexpr int kMaxWStages = 3;
-constexpr int kXStages = 2;
+constexpr int kMaxXStages = 4;
 
+// Shared-memory budget per token-tile width: narrow tiles fetch kSub activation k-blocks per
+// copy (a tensor copy costs a roughly fixed ~500 cycles), wide ones one k-block per copy.
 template <int kNT>
 struct Cfg {
+  static constexpr int kXSub = kNT <= 64 ? kSub : 1;
   static constexpr int kWStages = kNT <= 32 ? 3 : 2;
+  static constexpr int kXStages = kNT <= 64 ? 2 : (kNT == 128 ? 4 : 3);
+  static constexpr int kCStages = kNT <= 64 ? 5 : 4;
   static constexpr uint32_t kXBlock = kNT * BK * 2;  // one k-block of kNT activation rows
-  static constexpr uint32_t kXStage = kSub * kXBlock;
+  static constexpr uint32_t kXStage = kXSub * kXBlock;
   static constexpr uint32_t kDataBytes = kWStages * kWStage + kXStages * kXStage + kCStages * kCBlock;
   static constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
   static constexpr uint32_t kTmemCols = 2 * kNT < 32 ? 32 : 2 * kNT;  // two accumulators
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kWStages <= kMaxWStages && kXStages <= kMaxXStages && kCStages <= kMaxCStages, "barrier arrays");
 };
 
 struct Barriers {
   uint64_t w_full[kMaxWStages];
   uint64_t w_empty[kMaxWStages];
-  uint64_t x_full[kXStages];
-  uint64_t x_empty[kXStages];
-  uint64_t c_full[kCStages];
-  uint64_t c_empty[kCStages];
+  uint64_t x_full[kMaxXStages];
+  uint64_t x_empty[kMaxXStages];
+  uint64_t c_full[kMaxCStages];
+  uint64_t c_empty[kMaxCStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -79,14 +90,18 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block too large");
 
-// Work unit u -> feature tile t, K split s, weight k-blocks [kb0, kb1).
+// Work unit u -> tile t = (token tile m_blk, feature tile n_blk), K split s, weight k-blocks
+// [kb0, kb1). Token tiles vary fastest, so the tiles that share a weight tile run together
+// and re-read it from L2.
 struct Unit {
-  int t, s, kb0, kb1;
+  int t, m_blk, n_blk, s, kb0, kb1;
 };
 __device__ __forceinline__ Unit unit_of(const Args& a, int u) {
   Unit r;
   r.t = u / a.splits;
   r.s = u - r.t * a.splits;
+  r.n_blk = r.t / a.tiles_m;
+  r.m_blk = r.t - r.n_blk * a.tiles_m;
   r.kb0 = r.s * a.kb_per_split;
   r.kb1 = min(a.main_kb, r.kb0 + a.kb_per_split);
   return r;
@@ -101,26 +116,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap
       : "memory");
 }
 
-// Store 16 token values (tokens m0 .. m0 + 15, the ones below `mrows`) of one output feature,
-// i.e. of column `row` of the row-major output. Pairs of tokens share one packed conversion.
+// Store 16 token values (tokens tok0 + m0 .. tok0 + m0 + 15, those with m < `mrows`) of one
+// output feature, i.e. of column `row` of the row-major output. Pairs of tokens share one packed
+// conversion.
 template <int kV>
-__device__ __forceinline__ void store_tokens16(const Args& a, int row, const float (&v)[16], int m0, int mrows) {
+__device__ __forceinline__ void store_tokens16(const Args& a, int row, const float (&v)[16], int tok0, int m0,
+                                               int mrows) {
   if (a.out_kind == kV) {
-    uint16_t* out = static_cast<uint16_t*>(a.out);
+    uint16_t* out = static_cast<uint16_t*>(a.out) + static_cast<int64_t>(tok0) * a.ldo + row;
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
       const int m = m0 + j;
       if (m < mrows) {
         const uint32_t p = pack2_kind<kV>(v[j], v[j + 1]);
-        out[static_cast<int64_t>(m) * a.ldo + row] = static_cast<uint16_t>(p & 0xFFFFu);
-        if (m + 1 < mrows) out[static_cast<int64_t>(m + 1) * a.ldo + row] = static_cast<uint16_t>(p >> 16);
+        out[static_cast<int64_t>(m) * a.ldo] = static_cast<uint16_t>(p & 0xFFFFu);
+        if (m + 1 < mrows) out[static_cast<int64_t>(m + 1) * a.ldo] = static_cast<uint16_t>(p >> 16);
       }
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (m0 + j < mrows)
-        store_from_float(a.out, a.out_kind, static_cast<int64_t>(m0 + j) * a.ldo + row, round_to_kind(v[j], kV));
+        store_from_float(a.out, a.out_kind, static_cast<int64_t>(tok0 + m0 + j) * a.ldo + row, round_to_kind(v[j], kV));
   }
 }
 
@@ -135,25 +152,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* const base_ptr = smem_raw + (base - raw_base);
   const uint32_t w_smem = base;
   const uint32_t x_smem = w_smem + C::kWStages * kWStage;
-  const uint32_t c_smem = x_smem + kXStages * C::kXStage;
+  const uint32_t c_smem = x_smem + C::kXStages * C::kXStage;
   Barriers* bars = reinterpret_cast<Barriers*>(base_ptr + C::kDataBytes);
   auto bar = [&](uint64_t& b) { return smem_u32(&b); };
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_units = args.tiles_n * args.splits;
+  const int num_units = args.tiles_m * args.tiles_n * args.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kWStages; ++s) {
       mbar_init(bar(bars->w_full[s]), 1);
       mbar_init(bar(bars->w_empty[s]), kConvWarps);
     }
-    for (int s = 0; s < kXStages; ++s) {
+    for (int s = 0; s < C::kXStages; ++s) {
       mbar_init(bar(bars->x_full[s]), 1);
       mbar_init(bar(bars->x_empty[s]), 1);
     }
-    for (int s = 0; s < kCStages; ++s) {
+    for (int s = 0; s < C::kCStages; ++s) {
       mbar_init(bar(bars->c_full[s]), kGroupWarps);
       mbar_init(bar(bars->c_empty[s]), 1);
     }
@@ -178,7 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ producers
     // warp 0 streams the int8 weight ring, warp 2 the activation ring.
     const bool w_role = warp == 0;
-    const int nst = w_role ? C::kWStages : kXStages;
+    const int nst = w_role ? C::kWStages : C::kXStages;
+    const int per = w_role ? kSub : C::kXSub;  // k-blocks per copy
     if (lane == 0) tma_prefetch_desc(w_role ? &tm_w : &tm_x);
     int stage = 0;
     uint32_t phase = 0;
@@ -186,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       const Unit U = unit_of(args, u);
-      for (int kb = U.kb0; kb < U.kb1; kb += kSub) {
+      for (int kb = U.kb0; kb < U.kb1; kb += per) {
         const uint32_t empty_bar = w_role ? bar(bars->w_empty[stage]) : bar(bars->x_empty[stage]);
         if (!mbar_wait(empty_bar, phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
           ok = false;
@@ -198,15 +216,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t fb = bar(bars->w_full[stage]);
             mbar_arrive_expect_tx(fb, kWStage);
             if constexpr (!kDX) {
-              tma_load_3d(dst, &tm_w, fb, 0, U.t * BM, kb);  // [kSub][128 rows][64 B]
+              tma_load_3d(dst, &tm_w, fb, 0, U.n_blk * BM, kb);  // [kSub][128 rows][64 B]
             } else {
-              tma_load_2d(dst, &tm_w, fb, U.t * BM, kb * BK);  // [kSub * 64 rows][128 B], 128B swizzle
+              tma_load_2d(dst, &tm_w, fb, U.n_blk * BM, kb * BK);  // [kSub * 64 rows][128 B], 128B swizzle
             }
           } else {
             const uint32_t dst = x_smem + stage * C::kXStage;
             const uint32_t fb = bar(bars->x_full[stage]);
             mbar_arrive_expect_tx(fb, C::kXStage);
-            tma_load_3d(dst, &tm_x, fb, 0, 0, kb);  // [kSub][kNT rows][128 B], rows past M zero
+            tma_load_3d(dst, &tm_x, fb, 0, U.m_blk * kNT, kb);  // [kXSub][kNT rows][128 B], rows past M zero
           }
           used_mask |= 1u << stage;
           last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
@@ -248,43 +266,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kNT);
       bool first = true;
-      for (int kb = U.kb0; kb < U.kb1 && ok; kb += kSub) {
-        const int nsub = min(kSub, U.kb1 - kb);
-        if (!mbar_wait(bar(bars->x_full[xstage]), xphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
+      for (int kb = U.kb0; kb < U.kb1 && ok; ++kb) {
+        const int xsub = (kb - U.kb0) % C::kXSub;  // position in the activation stage
+        if (xsub == 0 &&
+            !mbar_wait(bar(bars->x_full[xstage]), xphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        for (int sub = 0; sub < nsub; ++sub) {
-          if (!mbar_wait(bar(bars->c_full[cstage]), cphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (lane == 0) {
-            const uint32_t c_base = c_smem + cstage * kCBlock;
-            const uint32_t x_base = x_smem + xstage * C::kXStage + sub * C::kXBlock;
-#pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              uint64_t adesc;
-              if constexpr (!kDX) {
-                adesc = umma_desc_sw128(c_base + kk * 32, 16, 1024);
-              } else {
-                adesc = umma_desc_sw128(c_base + kk * 2048, 8192, 1024);
-              }
-              const uint64_t bdesc = umma_desc_sw128(x_base + kk * 32, 16, 1024);
-              umma_f16(d_tmem, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
-            }
-            umma_commit(bar(bars->c_empty[cstage]));
-            issued_any = true;
-          }
-          first = false;
-          __syncwarp();
-          if (++cstage == kCStages) { cstage = 0; cphase ^= 1u; }
+        if (!mbar_wait(bar(bars->c_full[cstage]), cphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
+          ok = false;
+          break;
         }
-        if (!ok) break;
-        if (lane == 0) umma_commit(bar(bars->x_empty[xstage]));
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t c_base = c_smem + cstage * kCBlock;
+          const uint32_t x_base = x_smem + xstage * C::kXStage + xsub * C::kXBlock;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t adesc;
+            if constexpr (!kDX) {
+              adesc = umma_desc_sw128(c_base + kk * 32, 16, 1024);
+            } else {
+              adesc = umma_desc_sw128(c_base + kk * 2048, 8192, 1024);
+            }
+            const uint64_t bdesc = umma_desc_sw128(x_base + kk * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
+          }
+          umma_commit(bar(bars->c_empty[cstage]));
+          issued_any = true;
+        }
+        first = false;
         __syncwarp();
-        if (++xstage == kXStages) { xstage = 0; xphase ^= 1u; }
+        if (++cstage == C::kCStages) { cstage = 0; cphase ^= 1u; }
+        if (xsub == C::kXSub - 1 || kb == U.kb1 - 1) {
+          if (lane == 0) umma_commit(bar(bars->x_empty[xstage]));
+          __syncwarp();
+          if (++xstage == C::kXStages) { xstage = 0; xphase ^= 1u; }
+        }
       }
       if (!ok) break;
       if (lane == 0) umma_commit(bar(bars->acc_full[acc]));
@@ -305,7 +323,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int mrows = min(args.M, kNT);
     int it = 0;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
       const Unit U = unit_of(args, u);
@@ -314,7 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_EPILOGUE))
         break;
       tc_fence_after();
-      const int row = U.t * BM + q * 32 + lane;  // output feature
+      const int row = U.n_blk * BM + q * 32 + lane;  // output feature
+      const int tok0 = U.m_blk * kNT;                // first token (activation row) of the tile
+      const int mrows = min(kNT, args.M - tok0);
       const bool row_ok = row < args.Nc;
       float b = 0.0f;
       if constexpr (!kDX) {
@@ -336,62 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) + b;
-          store_tokens16<kV>(args, row, v, 16 * j, mrows);
+          store_tokens16<kV>(args, row, v, tok0, 16 * j, mrows);
         } else {
           // partial f32 sums of this split, [split][M][Nc]; lanes write consecutive features
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             if (16 * j + i < mrows)
-              args.partial[(static_cast<int64_t>(U.s) * args.M + 16 * j + i) * args.Nc + row] = __uint_as_float(r[i]);
+              args.partial[(static_cast<int64_t>(U.s) * args.M + tok0 + 16 * j + i) * args.Nc + row] = __uint_as_float(r[i]);
         }
       }
-      if (args.splits == 1) continue;
-      __threadfence();
-      __syncwarp();
-      int done = 0;
-      if (lane == 0) done = atomicAdd(args.counters + U.t * 4 + q, 1);
-      done = __shfl_sync(0xffffffffu, done, 0);
-      if (done != args.splits - 1) continue;
-      __threadfence();
-      if (row_ok) {
-        // Sum the splits in split order. The partials of 4 splits x 8 tokens are requested
-        // before any is added, so the reduction waits on one L2 round trip per 4 splits
-        // instead of one per split.
-        const int64_t split_stride = static_cast<int64_t>(args.M) * args.Nc;
-#pragma unroll 1
-        for (int j = 0; j < kNT / 16; ++j) {
-          if (16 * j >= mrows) break;
-          float v[16];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int m0 = 16 * j + 8 * h;
-            float acc8[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc8[i] = 0.0f;
-            const float* src = args.partial + static_cast<int64_t>(m0) * args.Nc + row;
-#pragma unroll 1
-            for (int sp0 = 0; sp0 < args.splits; sp0 += 4) {
-              float t[4][8];
-#pragma unroll
-              for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  t[u][i] = (sp0 + u < args.splits && m0 + i < mrows)
-                                ? __ldcg(src + (sp0 + u) * split_stride + static_cast<int64_t>(i) * args.Nc)
-                                : 0.0f;
-#pragma unroll
-              for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc8[i] += t[u][i];
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[8 * h + i] = acc8[i] + b;
-          }
-          store_tokens16<kV>(args, row, v, 16 * j, mrows);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) args.counters[U.t * 4 + q] = 0;  // ready for the next call
     }
   } else if (warp >= kConvWarp0) {
     // ------------------------------------------------------------------ converters
@@ -407,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       const Unit U = unit_of(args, u);
-      const int n0 = U.t * BM;
+      const int n0 = U.n_blk * BM;
       Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
 #pragma unroll
@@ -473,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(bar(bars->c_full[cstage]));
           }
           // every group walks every converted stage, so the ring positions stay in step
-          if (++cstage == kCStages) { cstage = 0; cphase ^= 1u; }
+          if (++cstage == C::kCStages) { cstage = 0; cphase ^= 1u; }
         }
         if (!ok) break;
         if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));
@@ -487,6 +459,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// Split-K epilogue: out[m, n] = round_v(sum_s partial[s, m, n] + round_v(bias[n])), the splits
+// added in order. A thread produces 8 consecutive features of one row: two 16-byte loads per
+// split and one 16-byte store, so every access is coalesced.
+template <int kV>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int Nc, const void* bias, int bias_kind,
+                         void* out, int out_kind, int64_t ldo) {
+  const int groups = (Nc + 7) / 8;
+  const int64_t total = static_cast<int64_t>(M) * groups;
+  const int64_t split_stride = static_cast<int64_t>(M) * Nc;
+  const bool vec_in = (Nc & 3) == 0;  // rows of 16-byte aligned float4s (the workspace is 256-byte aligned)
+  const bool vec_out = out_kind == kV && (ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / groups);
+    const int n0 = static_cast<int>(i - static_cast<int64_t>(m) * groups) * 8;
+    const bool full = n0 + 8 <= Nc;
+    const float* src = partial + static_cast<int64_t>(m) * Nc + n0;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    if (full && vec_in) {
+#pragma unroll 4
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4 a = __ldcs(reinterpret_cast<const float4*>(src + sp * split_stride));
+        const float4 b = __ldcs(reinterpret_cast<const float4*>(src + sp * split_stride) + 1);
+        v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+      }
+    } else {
+      for (int sp = 0; sp < splits; ++sp) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (n0 + j < Nc) v[j] += __ldcs(src + sp * split_stride + j);
+      }
+    }
+    if (bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < Nc) v[j] += round_to_kind(load_as_float(bias, bias_kind, n0 + j), kV);
+    }
+    const int64_t off = static_cast<int64_t>(m) * ldo + n0;
+    if (full && vec_out) {
+      const uint4 o = make_uint4(pack2_kind<kV>(v[0], v[1]), pack2_kind<kV>(v[2], v[3]), pack2_kind<kV>(v[4], v[5]),
+                                 pack2_kind<kV>(v[6], v[7]));
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + off) = o;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n0 + j < Nc) store_from_float(out, out_kind, off + j, round_to_kind(v[j], kV));
+    }
   }
 }
 
@@ -505,18 +531,29 @@ static int launch_typed(const CUtensorMap& tx, const CUtensorMap& tw, const Args
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] { attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes); });
   MOSS_CUDA_TRY(attr_err);
-  const int units = a.tiles_n * a.splits;
+  const int units = a.tiles_m * a.tiles_n * a.splits;
   const unsigned grid = static_cast<unsigned>(std::max(1, std::min(units, sm_count())));
   kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tx, tw, a);
   MOSS_CUDA_TRY(cudaGetLastError());
+  if (a.splits > 1) {
+    const int64_t total = static_cast<int64_t>(a.M) * ((a.Nc + 7) / 8);
+    const unsigned rgrid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * sm_count())));
+    splitk_reduce_kernel<kV><<<rgrid, 256, 0, stream>>>(a.partial, a.splits, a.M, a.Nc, kDX ? nullptr : a.bias, a.bias_kind,
+                                                        a.out, a.out_kind, a.ldo);
+    MOSS_CUDA_TRY(cudaGetLastError());
+  }
   return MOSS_OK;
 }
 
 template <bool kDX, int kV, bool kFast>
 static int launch_nt(int nt, const CUtensorMap& tx, const CUtensorMap& tw, const Args& a, cudaStream_t s) {
-  if (nt == 16) return launch_typed<kDX, kV, kFast, 16>(tx, tw, a, s);
-  if (nt == 32) return launch_typed<kDX, kV, kFast, 32>(tx, tw, a, s);
-  return launch_typed<kDX, kV, kFast, 64>(tx, tw, a, s);
+  switch (nt) {
+    case 16: return launch_typed<kDX, kV, kFast, 16>(tx, tw, a, s);
+    case 32: return launch_typed<kDX, kV, kFast, 32>(tx, tw, a, s);
+    case 64: return launch_typed<kDX, kV, kFast, 64>(tx, tw, a, s);
+    case 128: return launch_typed<kDX, kV, kFast, 128>(tx, tw, a, s);
+    default: return launch_typed<kDX, kV, kFast, 256>(tx, tw, a, s);
+  }
 }
 
 }  // namespace skinny
@@ -524,29 +561,39 @@ static int launch_nt(int nt, const CUtensorMap& tx, const CUtensorMap& tw, const
 SkinnyPlan plan_skinny(int64_t M, int64_t Nc, int64_t Kr, int sms) {
   using namespace skinny;
   SkinnyPlan p;
-  if (M <= 0 || M > kSkinnyMaxRows || Nc <= 0 || Kr <= 0) return p;
-  const int64_t tiles = (Nc + BM - 1) / BM;
+  if (M <= 0 || Nc <= 0 || Kr <= 0 || M > INT32_MAX) return p;
+  p.nt = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
+  const int64_t tiles_m = (M + p.nt - 1) / p.nt;
+  const int64_t tiles_n = (Nc + BM - 1) / BM;
+  const int64_t tiles = tiles_m * tiles_n;
   const int64_t main_kb = (Kr + BK - 1) / BK;
+  if (tiles > INT32_MAX / 64) return p;
   p.usable = true;
-  p.tiles = static_cast<int>(tiles);
-  p.nt = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  p.tiles_m = static_cast<int>(tiles_m);
+  p.tiles_n = static_cast<int>(tiles_n);
   p.splits = 1;
   p.kb_per_split = static_cast<int>(main_kb);
-  // Split K while the feature tiles fill less than ~3/4 of the GPU, keeping whole stages.
-  if (tiles * 4 < static_cast<int64_t>(sms) * 3) {
-    const int64_t want = std::min<int64_t>((sms + tiles - 1) / tiles, (main_kb + kSub - 1) / kSub);
-    if (want > 1) {
-      int64_t kps = (main_kb + want - 1) / want;
-      kps = (kps + kSub - 1) / kSub * kSub;
-      const int64_t splits = (main_kb + kps - 1) / kps;
-      if (splits > 1) {
-        p.splits = static_cast<int>(splits);
-        p.kb_per_split = static_cast<int>(kps);
-        p.partial_bytes = (static_cast<size_t>(splits) * M * Nc * 4 + 255) / 256 * 256;
-        p.counter_bytes = (static_cast<size_t>(tiles) * 4 * 4 + 255) / 256 * 256;
-      }
+  // Split K when it pays: a rough per-CTA time model in microseconds, per k-block (converter
+  // bound for narrow token tiles, MMA bound for 256) plus a fixed pipeline fill per wave of
+  // units, against the partials a split writes and the reduction kernel reads back.
+  const double t_kb = std::max(0.2, 0.27 * p.nt / 256.0);
+  auto waves = [&](int64_t units) { return static_cast<double>((units + sms - 1) / sms); };
+  double best = waves(tiles) * (main_kb * t_kb + 2.0);
+  const int64_t max_splits = std::min<int64_t>((main_kb + kSub - 1) / kSub, 64);
+  for (int64_t want = 2; want <= max_splits; ++want) {
+    int64_t kps = (main_kb + want - 1) / want;
+    kps = (kps + kSub - 1) / kSub * kSub;
+    const int64_t splits = (main_kb + kps - 1) / kps;
+    if (splits != want) continue;
+    const double cost = waves(tiles * splits) * (kps * t_kb + 2.0) + 2.0 +
+                        2.0 * static_cast<double>(splits) * M * Nc * 4.0 / 5.0e6;
+    if (cost < best) {
+      best = cost;
+      p.splits = static_cast<int>(splits);
+      p.kb_per_split = static_cast<int>(kps);
     }
   }
+  if (p.splits > 1) p.partial_bytes = (static_cast<size_t>(p.splits) * M * Nc * 4 + 255) / 256 * 256;
   return p;
 }
 
@@ -558,10 +605,10 @@ int launch_skinny(bool dx, int v_kind, bool fast, int nt, const Args& a, cudaStr
   memset(&tx, 0, sizeof(tx));
   memset(&tw, 0, sizeof(tw));
   {
-    // activations [M, Kr] viewed as {64, M, Kr / 64}: one box = kSub k-blocks of nt rows
+    // activations [M, Kr] viewed as {64, M, Kr / 64}: one box = kSub (nt <= 64) or 1 k-blocks of nt rows
     const uint64_t dims[3] = {BK, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.Kr / BK)};
     const uint64_t strides[2] = {static_cast<uint64_t>(a.lda) * 2, BK * 2};
-    const uint32_t box[3] = {BK, static_cast<uint32_t>(nt), kSub};
+    const uint32_t box[3] = {BK, static_cast<uint32_t>(nt), nt <= 64 ? static_cast<uint32_t>(kSub) : 1u};
     if (!make_map_nd(&tx, v_dt, 2, a.a, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return MOSS_ERR_UNSUPPORTED;
   }
   if (!dx) {

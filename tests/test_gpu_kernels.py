@@ -303,14 +303,20 @@ FEW_ROWS = [
     (32, 3072, 3072),
     (33, 2048, 520),     # 64-token tile, ragged features
     (64, 3072, 1536),
+    (100, 1024, 3072),   # 128-token tile
+    (128, 3072, 1536),
+    (200, 2048, 1280),   # 256-token tile, ragged
+    (300, 1024, 2560),   # two token tiles, the second ragged
+    (512, 1024, 3072),   # too few CTA-pair tiles: operand-swapped kernel with split-K
 ]
 
 
 @pytest.mark.parametrize("m,k,n", FEW_ROWS)
 @pytest.mark.parametrize("v_dtype", [torch.bfloat16, torch.float16])
 def test_few_row_kernel_forward_and_input_gradient(cuda_device, m, k, n, v_dtype):
-    """At most 64 rows run the operand-swapped kernel (weight as the 128-row MMA operand),
-    split over K when the feature tiles alone cannot occupy the GPU."""
+    """Problems with too few rows for the CTA-pair tiles run the operand-swapped kernel
+    (weight as the 128-row MMA operand, up to 256 tokens per tile), split over K when the
+    tiles alone cannot occupy the GPU."""
     v_kind = O.BF16 if v_dtype == torch.bfloat16 else O.F16
     x, q, s = _rand_problem(m, k, n, seed=1000 + m + n)
     bias = torch.randn(n, generator=torch.Generator().manual_seed(m)) * 0.5
