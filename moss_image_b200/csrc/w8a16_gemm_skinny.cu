@@ -54,8 +54,8 @@ constexpr int kThreads = (kConvWarp0 + kConvWarps) * 32;
 constexpr uint32_t kWBlock = BM * BK;          // 8 KB of int8 per k-block (both directions)
 constexpr uint32_t kWStage = kSub * kWBlock;   // 32 KB
 constexpr uint32_t kCBlock = BM * BK * 2;      // 16 KB converted operand per k-block
-constexpr int kMaxCStages = 5;
-constexpr int kMaxWStages = 3;
+constexpr int kMaxCStages = 7;
+constexpr int kMaxWStages = 4;
 constexpr int kMaxXStages = 4;
 
 // Shared-memory budget per token-tile width: narrow tiles fetch kSub activation k-blocks per
@@ -64,8 +64,10 @@ template <int kNT>
 struct Cfg {
   static constexpr int kXSub = kNT <= 64 ? kSub : 1;
   static constexpr int kWStages = kNT <= 32 ? 3 : 2;
-  static constexpr int kXStages = kNT <= 64 ? 2 : (kNT == 128 ? 4 : 3);
-  static constexpr int kCStages = kNT <= 64 ? 5 : 4;
+  static constexpr int kXStages = kNT == 128 ? 4 : 2;
+  // More converted stages than converter groups: a group then never waits for the MMA of its
+  // own previous k-block before converting the next one.
+  static constexpr int kCStages = kNT == 16 ? 7 : 6;
   static constexpr uint32_t kXBlock = kNT * BK * 2;  // one k-block of kNT activation rows
   static constexpr uint32_t kXStage = kXSub * kXBlock;
   static constexpr uint32_t kDataBytes = kWStages * kWStage + kXStages * kXStage + kCStages * kCBlock;
@@ -394,6 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        // Each warp releases the int8 stage as soon as its k-block is in registers, so the
+        // producer refills it while the decode, stores and fence are still running; warps with
+        // no k-block in a short final stage release it after the stage has landed.
+        bool released = false;
         for (int sub = 0; sub < nsub; ++sub) {
           if (sub == group) {
             if (!mbar_wait(bar(bars->c_empty[cstage]), cphase ^ 1u, abort_flag, args.status,
@@ -409,6 +415,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint2 qv[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) qv[i] = lds64(w_base + sub * kWBlock + (crow + 16 * i) * 64 + cch * 8);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));  // int8 bytes are in registers
+              released = true;
 #pragma unroll
               for (int i = 0; i < 8; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
 #pragma unroll
@@ -432,6 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int q16 = 4 * a + (cch >> 1);
                 qv[i] = lds64(w_base + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) + (cch & 1) * 8);
               }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));  // int8 bytes are in registers
+              released = true;
 #pragma unroll
               for (int i = 0; i < 8; ++i) o[i] = dec[i & 3].chunk8(qv[i], args.w_kind);
 #pragma unroll
@@ -448,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++cstage == C::kCStages) { cstage = 0; cphase ^= 1u; }
         }
         if (!ok) break;
-        if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));
+        if (!released && lane == 0) mbar_arrive(bar(bars->w_empty[stage]));
         if (++stage == C::kWStages) { stage = 0; phase ^= 1u; }
       }
     }

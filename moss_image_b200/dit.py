@@ -37,6 +37,10 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16):
+            # torch's fused kernel (f32 statistics, one rounding of the product); it needs the
+            # gain in the activation dtype
+            return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
         dtype = x.dtype
         h = x.float()
         h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.eps)
@@ -64,15 +68,16 @@ class SyntheticBlock(nn.Module):
         batch, seq, dim = tokens.shape
         modulation = self.adaln(F.silu(cond)).view(batch, 6, dim)
         shift_a, scale_a, gate_a, shift_f, scale_f, gate_f = (m.unsqueeze(1) for m in modulation.unbind(1))
-        h = self.norm1(tokens) * (1 + scale_a) + shift_a
+        # modulation and gated residuals as single fused multiply-adds
+        h = torch.addcmul(shift_a, self.norm1(tokens), 1 + scale_a)
         q = self.q_norm(self.proj["q"](h).unflatten(-1, (self.heads, -1)))
         k = self.k_norm(self.proj["k"](h).unflatten(-1, (self.heads, -1)))
         v = self.proj["v"](h).unflatten(-1, (self.heads, -1))
         attended = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
         attended = attended.transpose(1, 2).flatten(2)
-        tokens = tokens + self.proj["o"](attended) * gate_a
-        h = self.norm2(tokens) * (1 + scale_f) + shift_f
-        return tokens + self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")) * gate_f
+        tokens = torch.addcmul(tokens, self.proj["o"](attended), gate_a)
+        h = torch.addcmul(shift_f, self.norm2(tokens), 1 + scale_f)
+        return torch.addcmul(tokens, self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")), gate_f)
 
 
 class TimestepEmbedding(nn.Module):
