@@ -397,6 +397,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0, bstage = 0, astage = 0;
     uint32_t phase = 0, bphase = 0, aphase = 0;
     bool ok = true;
+    // forward: the row scales of the next tile are requested while this one is converted
+    float next_scale[8];
+    auto load_tile_scales = [&](int t_next) {
+      if constexpr (!kDX) {
+        int mb, nb;
+        tile_coords(t_next, args.tiles_m, args.tiles_n, mb, nb);
+        const int base_n = nb * kTileN + static_cast<int>(rank) * kHalf;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int gn = base_n + crow + 16 * i;
+          next_scale[i] = (t_next < num_tiles && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
+        }
+      }
+    };
+    load_tile_scales(pair_id);
     for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
       int m_blk, n_blk;
       tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
@@ -404,13 +419,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int gn = n0 + crow + 16 * i;
-          dec_f[i].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-        }
+        for (int i = 0; i < 8; ++i) dec_f[i].set(next_scale[i], args.w_kind);
+        load_tile_scales(t + num_pairs);
       }
       for (int si = 0; si < nsteps && ok; ++si) {
         const Step st = step_of(si, args.main_kb);
+        // grad-input: the row scales of this group's k-block depend only on the k-block index,
+        // so they are requested before the waits instead of inside the conversion chain
+        float dx_scale[4];
+        if constexpr (kDX) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int gn = (st.first_kb + group) * BK + crow + 16 * j;
+            dx_scale[j] = (!st.ext && group < st.nsub && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
+          }
+        }
         if (!mbar_wait(bar(bars->w_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
           ok = false;
           break;
@@ -454,10 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!st.ext) {
                 Dec<kV, kFast> dec[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const int gn = (st.first_kb + sub) * BK + crow + 16 * j;
-                  dec[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-                }
+                for (int j = 0; j < 4; ++j) dec[j].set(dx_scale[j], args.w_kind);
                 uint2 qv[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {

@@ -379,19 +379,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0, cstage = 0;
     uint32_t phase = 0, cphase = 0;
     bool ok = true;
+    // forward: the row scales of the next unit are requested while this one is converted
+    float next_scale[8];
+    auto load_unit_scales = [&](int u_next) {
+      if constexpr (!kDX) {
+        const int base_n = u_next < num_units ? unit_of(args, u_next).n_blk * BM : 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int gn = base_n + crow + 16 * i;
+          next_scale[i] = (u_next < num_units && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
+        }
+      }
+    };
+    load_unit_scales(blockIdx.x);
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       const Unit U = unit_of(args, u);
-      const int n0 = U.n_blk * BM;
       Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int gn = n0 + crow + 16 * i;
-          dec_f[i].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-        }
+        for (int i = 0; i < 8; ++i) dec_f[i].set(next_scale[i], args.w_kind);
+        load_unit_scales(u + gridDim.x);
       }
       for (int kb = U.kb0; kb < U.kb1 && ok; kb += kSub) {
         const int nsub = min(kSub, U.kb1 - kb);
+        // grad-input: request this group's row scales before the waits (they depend only on
+        // the k-block index), not inside the conversion chain
+        float dx_scale[4];
+        if constexpr (kDX) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int gn = (kb + group) * BK + crow + 16 * j;
+            dx_scale[j] = (group < nsub && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
+          }
+        }
         if (!mbar_wait(bar(bars->w_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
           ok = false;
           break;
@@ -430,10 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // the stage holds kSub * 64 reduction rows of 128 bytes (128B swizzle).
               Dec<kV, kFast> dec[4];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int gn = (kb + sub) * BK + crow + 16 * j;
-                dec[j].set(gn < args.w_rows ? args.scale[gn] : 0.0f, args.w_kind);
-              }
+              for (int j = 0; j < 4; ++j) dec[j].set(dx_scale[j], args.w_kind);
               uint2 qv[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
