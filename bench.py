@@ -48,7 +48,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--batch", type=int, default=BATCH)
     p.add_argument("--no-offload", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx"], default=None)
+    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx"], default=None)
+    p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
     p.add_argument("--m", type=int, default=9216)
     p.add_argument("--k", type=int, default=3072)
     p.add_argument("--n", type=int, default=3072)
@@ -230,6 +231,17 @@ def run_kernel(args: argparse.Namespace) -> None:
     if args.kernel == "gemm_fwd":
         x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.int8_linear_forward(x, q, s, None, torch.bfloat16, torch.bfloat16)  # noqa: E731
+    elif args.kernel == "hadamard":
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        fn = lambda: qk.hadamard_transform(x, args.group, out=y)  # noqa: E731
+    elif args.kernel == "convrot_fwd":
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        fn = lambda: qk.convrot_forward(x, q, s, None, torch.bfloat16, torch.bfloat16, args.group)  # noqa: E731
+    elif args.kernel == "convrot_dx":
+        dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
+        fn = lambda: qk.convrot_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16,  # noqa: E731
+                                         args.group)
     else:
         dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)  # noqa: E731
@@ -244,8 +256,13 @@ def run_kernel(args: argparse.Namespace) -> None:
     torch.cuda.synchronize()
     ms = start.elapsed_time(end) / args.steps
     qk.check_device_status(dev)
-    print(json.dumps({"kernel": args.kernel, "m": m, "k": k, "n": n, "us": ms * 1e3,
-                      "tflops": 2.0 * m * n * k / ms / 1e9}), flush=True)
+    line = {"kernel": args.kernel, "m": m, "k": k, "n": n, "us": ms * 1e3}
+    if args.kernel == "hadamard":
+        line["gbs"] = 2.0 * m * k * 2 / ms / 1e6  # one bf16 read and one write
+        line["group"] = args.group
+    else:
+        line["tflops"] = 2.0 * m * n * k / ms / 1e9
+    print(json.dumps(line), flush=True)
 
 
 def run_sweep(args: argparse.Namespace) -> None:

@@ -344,3 +344,120 @@ def dequantize_weight(weight: torch.Tensor, scale: torch.Tensor, dtype: torch.dt
     )
     _lib.check(rc, "moss_w8_dequantize")
     return out
+
+
+# ------------------------------------------------------------------ ConvRot (grouped Hadamard)
+# Rows rotated per call of the ConvRot launchers: bounds the temporary rotated activations at
+# 32 Mi elements whatever the token count (one chunk for any step of the benchmark).
+_CONVROT_WORKSPACE_ELEMENTS = 32 << 20
+
+
+def hadamard_transform(
+    tokens: torch.Tensor,
+    group_size: int,
+    *,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Grouped normalised Hadamard rotation of a contiguous CUDA matrix in one pass.
+
+    Reference: ``triton_hadamard_transform``, training/quant_kernels.py:387-426 (same
+    arguments and errors; ``workspace`` is accepted for compatibility and unused: all
+    stages run on chip). ``out`` may be ``tokens`` itself (in place).
+    """
+    if tokens.ndim != 2 or not tokens.is_contiguous():
+        raise ValueError("Triton Hadamard input must be a contiguous matrix.")
+    if tokens.shape[1] % group_size:
+        raise ValueError("Input width must be divisible by Hadamard group size.")
+    if out is None:
+        out = torch.empty_like(tokens)
+    if out.shape != tokens.shape or out.dtype != tokens.dtype or not out.is_contiguous():
+        raise ValueError("Triton Hadamard output must match its contiguous input.")
+    if tokens.device.type != "cuda":
+        raise RuntimeError("int8 quantized backend is unavailable: the input is not on CUDA.")
+    rc = _lib.library().moss_hadamard_rotate(
+        _lib.ptr(tokens), _lib.dtype_code(tokens.dtype), tokens.shape[0], tokens.shape[1], int(group_size),
+        _lib.ptr(out), _lib.stream_handle(tokens.device),
+    )
+    _lib.check(rc, "moss_hadamard_rotate")
+    return out
+
+
+def _convrot_chunk_rows(in_features: int, rows: int) -> int:
+    return min(rows, max(1, _CONVROT_WORKSPACE_ELEMENTS // in_features))
+
+
+def convrot_forward(
+    tokens: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    bias: torch.Tensor | None,
+    output_dtype: torch.dtype,
+    weight_dtype: torch.dtype,
+    group_size: int,
+) -> torch.Tensor:
+    """ConvRot forward ``(x H) dec(W H)^T + b``: rotate the activations, then the int8 GEMM.
+
+    Reference: ``triton_convrot_forward``, training/quant_kernels.py:433-466. The rotation
+    is one on-chip pass per chunk of rows (the reference runs one kernel per radix stage).
+    """
+    matrix = _matrix_view(tokens)
+    if not matrix.is_contiguous():
+        matrix = matrix.contiguous()
+    rows, in_features = matrix.shape
+    out_features = weight.shape[0]
+    output = torch.empty((rows, out_features), device=tokens.device, dtype=output_dtype)
+    if rows == 0:
+        return output.reshape(*tokens.shape[:-1], out_features)
+    chunk_rows = _convrot_chunk_rows(in_features, rows)
+    rotated = torch.empty((chunk_rows, in_features), device=tokens.device, dtype=matrix.dtype)
+    for start in range(0, rows, chunk_rows):
+        count = min(chunk_rows, rows - start)
+        rotated_chunk = rotated[:count]
+        hadamard_transform(matrix[start : start + count], group_size, out=rotated_chunk)
+        gemm_input = rotated_chunk if rotated_chunk.dtype == weight_dtype else rotated_chunk.to(weight_dtype)
+        int8_linear_forward(gemm_input, weight, scale, bias, output_dtype, weight_dtype,
+                            out=output[start : start + count])
+    return output.reshape(*tokens.shape[:-1], out_features)
+
+
+def convrot_backward(
+    gradient: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    input_shape: torch.Size,
+    input_dtype: torch.dtype,
+    weight_dtype: torch.dtype,
+    group_size: int,
+) -> torch.Tensor:
+    """ConvRot input gradient ``H (dY dec(W H))``: the int8 grad-input GEMM, then the rotation
+    in place on its output (H is symmetric and orthonormal).
+
+    Reference: ``triton_convrot_backward``, training/quant_kernels.py:469-504.
+    """
+    matrix = _matrix_view(gradient.contiguous())
+    rows = matrix.shape[0]
+    in_features = weight.shape[1]
+    grad_input = int8_linear_backward(matrix, weight, scale, torch.Size((rows, in_features)), input_dtype,
+                                      weight_dtype)
+    if rows:
+        hadamard_transform(grad_input, group_size, out=grad_input)
+    return grad_input.reshape(input_shape)
+
+
+def convrot_workspace_bound_bytes(in_features: int, dtype: torch.dtype) -> int:
+    """Upper bound for the temporary rotated activations of one ConvRot forward call.
+
+    Reference: training/quant_kernels.py:507-513 (the reference bounds two stage buffers;
+    here only the rotated chunk exists, for a larger chunk).
+    """
+    if in_features < 1:
+        raise ValueError("input width must be positive")
+    element_size = torch.empty((), dtype=dtype).element_size()
+    rows = max(1, _CONVROT_WORKSPACE_ELEMENTS // in_features)
+    return rows * in_features * element_size
+
+
+triton_hadamard_transform = hadamard_transform
+triton_convrot_forward = convrot_forward
+triton_convrot_backward = convrot_backward

@@ -44,6 +44,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_offload_view.restype = i32
         L.oracle_gather.argtypes = [vp, i64, i32, vp, vp, vp]
         L.oracle_round.argtypes = [f32, i32]
+        L.oracle_hadamard.argtypes = [vp, i64, i64, i64, i32, vp]
         L.oracle_round.restype = f32
         _lib = L
     return _lib
@@ -193,3 +194,15 @@ def gather(storage: np.ndarray, esize: int, shape: tuple[int, ...], stride: tupl
     lib().oracle_gather(base.ctypes.data_as(ctypes.c_void_p), esize, nd, ctypes.cast(sh, ctypes.c_void_p),
                         ctypes.cast(st, ctypes.c_void_p), out.ctypes.data_as(ctypes.c_void_p))
     return out.tobytes()
+
+
+def hadamard(x: np.ndarray, group: int, kind: int) -> np.ndarray:
+    """Grouped normalised Hadamard rotation of the last dimension, each stage rounded to
+    ``kind`` (w8_oracle.c: oracle_hadamard; reference training/quant_kernels.py:231-277,
+    :376-426)."""
+    a = np.ascontiguousarray(x, dtype=np.float32)
+    cols = a.shape[-1]
+    rows = a.size // cols if cols else 0
+    out = np.empty_like(a)
+    lib().oracle_hadamard(_p(a), rows, cols, group, kind, _p(out))
+    return out

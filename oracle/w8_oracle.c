@@ -217,3 +217,48 @@ void oracle_gather(const uint8_t* src, int64_t esize, int ndim, const int64_t* s
     memcpy(dst + i * esize, src + off * esize, (size_t)esize);
   }
 }
+
+/*
+ * Grouped normalised Hadamard rotation (ConvRot), as the reference's staged transform
+ * computes it (training/quant_kernels.py:231-277 for one stage, :376-426 for the stage
+ * order): radix-4 stages at strides 1, 4, 16, ... while 4 * stride <= group, then one radix-2
+ * stage if log2(group) is odd. Each stage reads the previous stage's values, computes in f32
+ *   radix 4: total = ((a + b) + c) + d; out[digit] = (total - 2 * {d, c, b, a}[digit]) * 0.5
+ *   radix 2: out = (a + b) * 0.70710678f, (a - b) * 0.70710678f
+ * and rounds to `kind` (the reference stores every stage in the tensor's dtype).
+ * In place is allowed (y == x).
+ */
+void oracle_hadamard(const float* x, int64_t rows, int64_t cols, int64_t group, int kind, float* y) {
+  if (y != x) memcpy(y, x, (size_t)(rows * cols) * sizeof(float));
+  if (group <= 1) return;
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t g0 = 0; g0 < cols; g0 += group) {
+      float* v = y + r * cols + g0;
+      int64_t stride = 1;
+      while (stride * 4 <= group) {
+        for (int64_t base = 0; base < group; base += 4 * stride) {
+          for (int64_t p = 0; p < stride; ++p) {
+            const float a = v[base + p], b = v[base + p + stride];
+            const float c = v[base + p + 2 * stride], d = v[base + p + 3 * stride];
+            const float total = ((a + b) + c) + d;
+            v[base + p] = oracle_round((total - 2.0f * d) * 0.5f, kind);
+            v[base + p + stride] = oracle_round((total - 2.0f * c) * 0.5f, kind);
+            v[base + p + 2 * stride] = oracle_round((total - 2.0f * b) * 0.5f, kind);
+            v[base + p + 3 * stride] = oracle_round((total - 2.0f * a) * 0.5f, kind);
+          }
+        }
+        stride *= 4;
+      }
+      if (stride < group) {
+        const float h = 0.7071067811865476f;
+        for (int64_t base = 0; base < group; base += 2 * stride) {
+          for (int64_t p = 0; p < stride; ++p) {
+            const float a = v[base + p], b = v[base + p + stride];
+            v[base + p] = oracle_round((a + b) * h, kind);
+            v[base + p + stride] = oracle_round((a - b) * h, kind);
+          }
+        }
+      }
+    }
+  }
+}

@@ -12,7 +12,10 @@ and records, on CPU:
   plus the bit-exact decode/bias-rounding known-answer case of the reference GPU test
   (training/tests/test_quant_kernels.py:85-129) evaluated with the reference eager path;
 * ``_offload_view`` payload shapes for padded, expanded, overlapping, transposed and
-  sliced layouts (training/tests/test_packed_features.py:201-235 and more).
+  sliced layouts (training/tests/test_packed_features.py:201-235 and more);
+* ConvRot (``training.convrot``): ``rotate_hadamard`` outputs in f32 and f64 for every
+  group size from 1 to 512, ``effective_group_size`` answers, and the codes, scales,
+  rotated weights, eager outputs and input gradients of ``FrozenConvRotLinear``.
 
 Outputs: tests/golden/golden.npz (small arrays) and tests/golden/golden.json (hashes and
 metadata). The GPU box never runs this script; the tests read the committed outputs.
@@ -182,6 +185,42 @@ def main() -> None:
             "name": name, "shape": list(shape), "stride": list(stride),
             "payload_shape": None if result is None else list(result[1]),
         })
+
+    # ---------------------------------------------------------------- ConvRot
+    from training.convrot import FrozenConvRotLinear, effective_group_size, rotate_hadamard  # noqa: E402
+
+    for group in (1, 2, 4, 8, 16, 32, 64, 128, 256, 512):
+        gen = torch.Generator().manual_seed(500 + group)
+        x = torch.randn(3, 2 * group, generator=gen)
+        arrays[f"hadamard.g{group}.x"] = x.numpy()
+        arrays[f"hadamard.g{group}.y32"] = rotate_hadamard(x, group).numpy()
+        arrays[f"hadamard.g{group}.y64"] = rotate_hadamard(x.double(), group).numpy()
+    meta["effective_group_size"] = [
+        [width, req, effective_group_size(width, req)]
+        for width, req in [(48, 256), (17, 256), (3072, 256), (12288, 256), (1000, 256), (1024, 512),
+                           (96, 64), (5, 4), (256, 1), (24, 8)]
+    ]
+    for name, dtype, width, out_f, group in [("convrot_f32", torch.float32, 256, 37, 256),
+                                            ("convrot_bf16", torch.bfloat16, 256, 37, 64),
+                                            ("convrot_g16", torch.float32, 48, 8, 256)]:
+        torch.manual_seed(91)
+        base = nn.Linear(width, out_f).to(dtype).requires_grad_(False)
+        module = FrozenConvRotLinear(base, group)
+        arrays[f"{name}.w"] = to_np(base.weight.float())
+        arrays[f"{name}.bias"] = to_np(base.bias.float())
+        arrays[f"{name}.rotated"] = rotate_hadamard(base.weight.detach().float(), module.group_size).numpy()
+        arrays[f"{name}.q"] = module.weight_int8.numpy()
+        arrays[f"{name}.s"] = module.weight_scale.numpy()
+        tokens = torch.randn(2, 5, width).to(dtype).requires_grad_(True)
+        out = module(tokens)
+        grad = torch.randn_like(out)
+        out.backward(grad)
+        arrays[f"{name}.x"] = to_np(tokens.float())
+        arrays[f"{name}.y"] = to_np(out.float())
+        arrays[f"{name}.dy"] = to_np(grad.float())
+        arrays[f"{name}.dx"] = to_np(tokens.grad.float())
+        meta["cases"][name] = {"dtype": str(dtype).split(".")[-1], "group": module.group_size,
+                               "rotation_group_size": int(module.rotation_group_size.item())}
 
     np.savez_compressed(HERE / "golden.npz", **arrays)
     (HERE / "golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
