@@ -163,6 +163,21 @@ MOSS_API int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t
                        moss_stream_t stream);
 
 /*
+ * Grouped normalised Hadamard rotation of the last dimension (ConvRot), y = x . H with H
+ * block-diagonal in `group`-sized blocks (a power of two, at most 8192) built from the
+ * regular H4 and one H2 factor for odd log2(group). H is symmetric and orthonormal, so the
+ * same call rotates activations forward and input gradients back. Every radix stage is
+ * computed in f32 and rounded to the tensor's dtype, as the reference's staged transform does;
+ * all stages run in one pass. Replaces triton_hadamard_transform
+ * (training/quant_kernels.py:387-426) and its stage kernels (:231-277); eager equivalent
+ * rotate_hadamard (training/convrot.py:36-63).
+ *   x, y   device [rows, cols] contiguous in dtype (F16, BF16 or F32); y == x is allowed,
+ *          otherwise the two must not overlap; cols % group == 0
+ */
+MOSS_API int moss_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_t cols, int64_t group, void* y,
+                         moss_stream_t stream);
+
+/*
  * Dense gather of a strided (non-overlapping) view into a contiguous buffer, and the
  * inverse scatter. Used by the activation offload to turn the payload views of
  * _offload_view (training/activation_offload.py:32-61) into one copy-engine transfer and
