@@ -19,6 +19,10 @@ sampled during the timed region, and the number of this library's kernel launche
 only) and prints the same kind of line with ``"impl": "reference"``.
 ``--kernel gemm_fwd|gemm_dx --m M --k K --n N`` runs only the int8 GEMM (profiling aid).
 ``--sweep`` runs the GEMM sweep (M x (K, N) grid) and prints one JSON line per case.
+``--blocks-to-swap N`` streams the frozen int8 weights of the last N blocks from pinned host
+memory through the block stager (``place_model(..., block_swap_mode="async")``) and adds a
+``block_swap`` object (copy-engine GB/s against the host link); ``--img-tokens``/``--txt-tokens``
+change the per-sample token counts (e.g. 16384 + 4096 for 2048^2 images).
 """
 
 from __future__ import annotations
@@ -47,6 +51,10 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--depth", type=int, default=DEPTH)
     p.add_argument("--batch", type=int, default=BATCH)
     p.add_argument("--no-offload", action="store_true")
+    p.add_argument("--blocks-to-swap", type=int, default=0,
+                   help="stream the frozen int8 weights of the last N blocks from pinned host memory (async)")
+    p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
+    p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx"], default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
@@ -171,6 +179,39 @@ def load_traffic(kind: str) -> float | None:
         except (KeyError, ValueError):
             return None
     return None
+
+
+def host_link_gbs(dev, nbytes: int = 256 << 20, reps: int = 5) -> float:
+    """Best pinned-host -> device copy rate of one plain copy-engine transfer (GB/s)."""
+    import torch
+
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    device = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = float("inf")
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        device.copy_(host, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = min(best, a.elapsed_time(b))
+    return nbytes / (best * 1e-3) / 1e9
+
+
+def block_swap_summary(before: dict, after: dict, steps: int, elapsed_ms: float, dev) -> dict:
+    """Streamed-weight traffic of the timed region against the host link's copy rate."""
+    copies = after["copies"] - before["copies"]
+    nbytes = after["bytes"] - before["bytes"]
+    copy_ms = after["copy_ms"] - before["copy_ms"]
+    timed = after["timed_bytes"] - before["timed_bytes"]
+    link = host_link_gbs(dev)
+    engine = timed / (copy_ms * 1e-3) / 1e9 if copy_ms > 0 else None
+    return {"copies_per_step": copies / steps, "bytes_per_step": nbytes / steps,
+            "copy_engine_gbs": engine, "host_link_gbs": link,
+            "frac_of_host_link": engine / link if engine else None,
+            "link_busy_frac_of_step": copy_ms / elapsed_ms,
+            "note": "copy_engine_gbs: block bytes / summed copy time of the stager's H2D transfers (CUDA events on "
+                    "its copy stream); host_link_gbs: best plain 256 MiB pinned->device copy on an idle GPU"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
@@ -334,16 +375,24 @@ def run_train(args: argparse.Namespace) -> None:
 
     model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0)
     model.train()
+    streamer = None
+    if args.blocks_to_swap:
+        from moss_image_b200.memory import place_model
+
+        place_model(model, dev, args.blocks_to_swap, block_swap_mode="async")
+        streamer = model.block_swap_manager
+        torch.cuda.empty_cache()
     model.activation_offload = not args.no_offload
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
     reducer = GradAllReducer(params)
 
-    seq = IMG_TOKENS + TXT_TOKENS
+    img_tokens, txt_tokens = args.img_tokens, args.txt_tokens
+    seq = img_tokens + txt_tokens
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    latents = torch.randn(args.batch, IMG_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
-    text = torch.randn(args.batch, TXT_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
-    noise = torch.randn(args.batch, IMG_TOKENS, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    latents = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    text = torch.randn(args.batch, txt_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    noise = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
     t = torch.rand(args.batch, device=dev, generator=gen)
     host = [x.cpu().pin_memory() for x in (latents, text, noise, t)]
     h2d_bytes = sum(x.numel() * x.element_size() for x in host)
@@ -369,6 +418,7 @@ def run_train(args: argparse.Namespace) -> None:
     qk.check_device_status(dev)
     ring = ao.offload_ring(dev)
     stats0 = ring.stats()
+    swap0 = streamer.copy_statistics() if streamer is not None else None
 
     timer = GemmTimer()
     qk.set_launch_observer(timer)
@@ -387,6 +437,7 @@ def run_train(args: argparse.Namespace) -> None:
     clock_info = clocks.stop()
     elapsed_ms = start.elapsed_time(end)
     stats1 = ring.stats()
+    swap1 = streamer.copy_statistics() if streamer is not None else None
     gemm = timer.summary()
 
     # e2e: inputs copied from pinned host buffers each step, loss read back each step
@@ -437,9 +488,11 @@ def run_train(args: argparse.Namespace) -> None:
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": (f"{args.depth}-block synthetic DiT int8-W LoRA training step per GPU (batch "
-                                    f"{args.batch} x ({IMG_TOKENS} img + {TXT_TOKENS} txt) tokens, width {DIM}, MLP {MLP} "
+                                    f"{args.batch} x ({img_tokens} img + {txt_tokens} txt) tokens, width {DIM}, MLP {MLP} "
                                     f"GELU, per-block adaLN {DIM}->{6 * DIM}, LoRA r{RANK} q/k/v/o, grad checkpointing, "
-                                    f"activation offload {'on' if model.activation_offload else 'off'})"),
+                                    f"activation offload {'on' if model.activation_offload else 'off'}"
+                                    + (f", int8 blocks streamed from pinned host: last {args.blocks_to_swap}"
+                                       if args.blocks_to_swap else "") + ")"),
                        "global_batch": world * args.batch, "seq_len": seq, "parallelism": f"dp{world}",
                        "l2": "no flush: per-step working set (GBs of weights/activations) exceeds the 126 MB L2"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d_bytes,
@@ -454,6 +507,9 @@ def run_train(args: argparse.Namespace) -> None:
             "gpu_launches_note": "int8 GEMM launches (fwd + dx) of libmoss_w8.so in the timed region",
             "loss_last": losses[-1] if losses else None,
         }
+        if streamer is not None:
+            line["config"]["blocks_to_swap"] = args.blocks_to_swap
+            line["block_swap"] = block_swap_summary(swap0, swap1, args.steps, elapsed_ms, dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
         print(json.dumps(line), flush=True)

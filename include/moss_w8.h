@@ -45,6 +45,7 @@ typedef struct CUstream_st* moss_stream_t; /* == cudaStream_t */
 #define MOSS_ERR_CUDA 3
 #define MOSS_ERR_RING_FULL 4
 #define MOSS_ERR_NOT_FOUND 5
+#define MOSS_ERR_BUSY 6
 
 /* device status bits */
 #define MOSS_STATUS_NONFINITE_WEIGHT 0x1
@@ -214,6 +215,48 @@ MOSS_API int moss_offload_host_ptr(void* ring, int64_t ticket, void** host);
 /* Counters: bytes packed, bytes restored, live tickets, reserved pinned bytes. */
 MOSS_API int moss_offload_stats(void* ring, uint64_t* d2h_bytes, uint64_t* h2d_bytes, int64_t* live,
                        uint64_t* pinned_bytes);
+
+/*
+ * Frozen-block stager: the staging-slot state machine of the asynchronous block swap
+ * (replaces AsyncBlockStreamer._choose_slot/_stage/_run/_record_*_use/close,
+ * training/memory.py:143-255,335-360). Each registered block is one packed pinned-host
+ * master (the frozen parameters and buffers of a transformer block, training/memory.py:
+ * 442-471); a stage is one H2D copy of a master into a device slot on the caller's copy
+ * stream. Slot memory is supplied by the caller with moss_block_stager_set_slot.
+ * Events fence the copies: the copy into a slot waits for the last release of that slot,
+ * and a lease makes the compute stream wait for the slot's copy.
+ */
+MOSS_API int moss_block_stager_create(int device, int num_slots, moss_stream_t copy, void** stager);
+/* Waits for the copy stream and every slot's last release, then frees the stager.
+ * MOSS_ERR_BUSY (nothing freed) while a slot is leased, unless `force` is non-zero. */
+MOSS_API int moss_block_stager_destroy(void* stager, int force);
+/* Register a pinned host master of nbytes; returns its block id (0, 1, ...). */
+MOSS_API int moss_block_stager_add_block(void* stager, const void* host, size_t nbytes, int64_t* block);
+/* Give slot `slot` device memory of `capacity` bytes (caller-owned; 256-byte aligned). */
+MOSS_API int moss_block_stager_set_slot(void* stager, int slot, void* device, size_t capacity);
+/* The slot that holds `block`, else an empty slot, else the first slot neither leased nor
+ * holding one of the protected blocks. MOSS_ERR_BUSY if there is none. No state changes. */
+MOSS_API int moss_block_stager_select(void* stager, int64_t block, const int64_t* protected_blocks, int n_protected,
+                             int* slot);
+/* Make `slot` hold `block`: no-op if it already does, otherwise enqueue the H2D copy on the
+ * copy stream behind the slot's last release and advance the slot's generation. */
+MOSS_API int moss_block_stager_stage(void* stager, int64_t block, int slot, uint64_t* generation);
+/* Lease a slot for a block invocation: `compute` waits for the slot's copy.
+ * MOSS_ERR_BUSY if the slot is already leased. */
+MOSS_API int moss_block_stager_lease(void* stager, int slot, moss_stream_t compute, uint64_t* generation);
+/* Keep a leased slot leased past the invocation (a checkpoint recomputation whose block
+ * backward has not run yet); its release comes from release(). */
+MOSS_API int moss_block_stager_hold(void* stager, int slot);
+/* Record the slot's release on `stream` and drop the lease. With block >= 0 the slot must
+ * still hold that block at that generation (MOSS_ERR_NOT_FOUND otherwise). */
+MOSS_API int moss_block_stager_release(void* stager, int slot, int64_t block, uint64_t generation,
+                              moss_stream_t stream);
+/* Resident block (-1 if none), generation and lease flag of a slot. */
+MOSS_API int moss_block_stager_slot_info(void* stager, int slot, int64_t* block, uint64_t* generation, int* leased);
+/* Counters: copies and bytes staged, peak resident blocks; with copy_ms/timed_bytes
+ * non-null, waits for the outstanding copies and returns their summed copy-engine time. */
+MOSS_API int moss_block_stager_stats(void* stager, uint64_t* copies, uint64_t* bytes, int* peak_resident,
+                            double* copy_ms, uint64_t* timed_bytes);
 
 #ifdef __cplusplus
 }

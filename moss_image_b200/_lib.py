@@ -24,6 +24,7 @@ MOSS_ERR_UNSUPPORTED = 2
 MOSS_ERR_CUDA = 3
 MOSS_ERR_RING_FULL = 4
 MOSS_ERR_NOT_FOUND = 5
+MOSS_ERR_BUSY = 6
 
 NOALLOC_SCRATCH_BYTES = 4 << 20  # MOSS_W8A16_NOALLOC_SCRATCH_BYTES
 
@@ -69,6 +70,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i64),
          ctypes.POINTER(ctypes.c_uint64)],
+    ),
+    "moss_block_stager_create": (_i32, [_i32, _i32, _vp, ctypes.POINTER(_vp)]),
+    "moss_block_stager_destroy": (_i32, [_vp, _i32]),
+    "moss_block_stager_add_block": (_i32, [_vp, _vp, _sz, ctypes.POINTER(_i64)]),
+    "moss_block_stager_set_slot": (_i32, [_vp, _i32, _vp, _sz]),
+    "moss_block_stager_select": (_i32, [_vp, _i64, ctypes.POINTER(_i64), _i32, ctypes.POINTER(_i32)]),
+    "moss_block_stager_stage": (_i32, [_vp, _i64, _i32, ctypes.POINTER(ctypes.c_uint64)]),
+    "moss_block_stager_lease": (_i32, [_vp, _i32, _vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "moss_block_stager_hold": (_i32, [_vp, _i32]),
+    "moss_block_stager_release": (_i32, [_vp, _i32, _i64, ctypes.c_uint64, _vp]),
+    "moss_block_stager_slot_info": (
+        _i32, [_vp, _i32, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
+    "moss_block_stager_stats": (
+        _i32,
+        [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32),
+         ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64)],
     ),
 }
 

@@ -101,6 +101,9 @@ class FrozenConvRotLinear(FrozenInt8Linear):
     Reference: training/convrot.py:96-150.
     """
 
+    # the GEMM sees x H, not x: an adapter's update is added after the rotated product
+    fuses_lora = False
+
     def __init__(self, linear: nn.Linear, group_size: int = 256, *, backend: str = "eager") -> None:
         if any(parameter.requires_grad for parameter in linear.parameters()):
             raise ValueError("Freeze the base linear before ConvRot quantization (LoRA only).")

@@ -25,6 +25,7 @@ from torch.utils.checkpoint import checkpoint
 
 from .activation_offload import activation_cpu_offload
 from .lora import LoRALinear
+from .memory import offloaded_block
 from .quantization import quantize_frozen_linears
 
 
@@ -108,15 +109,42 @@ class SyntheticDiT(nn.Module):
         self.gradient_checkpointing = gradient_checkpointing
         self.activation_offload = False
 
-    def forward(self, tokens: torch.Tensor, timestep: torch.Tensor) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, timestep: torch.Tensor, skip_layers: tuple[int, ...] = ()) -> torch.Tensor:
         with activation_cpu_offload(self, self.activation_offload, tokens.device):
             cond = self.time_embedding(timestep).to(tokens.dtype)
-            for layer in self.layers:
-                if self.gradient_checkpointing and self.training and torch.is_grad_enabled():
-                    tokens = checkpoint(layer, tokens, cond, use_reentrant=False)
-                else:
-                    tokens = layer(tokens, cond)
+            tokens = self._run_layers(tokens, cond, frozenset(skip_layers))
             return self.final_norm(tokens)
+
+    def _run_layers(self, tokens: torch.Tensor, cond: torch.Tensor, skipped: frozenset[int]) -> torch.Tensor:
+        """Resident, synchronously swapped or streamed blocks, as ``place_model`` left them.
+
+        Mirrors training/model.py:672-709: blocks at or past ``len(layers) - blocks_to_swap``
+        run through the streamer (prefetching the next streamed block in the direction of
+        traversal, checkpointed whenever gradients are enabled) or, without a streamer,
+        from their CPU masters; the others are checkpointed when training.
+        """
+        boundary = len(self.layers) - getattr(self, "blocks_to_swap", 0)
+        manager = getattr(self, "block_swap_manager", None)
+        streamed = [index for index in range(boundary, len(self.layers)) if index not in skipped]
+        position = {index: slot for slot, index in enumerate(streamed)}
+        for index, layer in enumerate(self.layers):
+            if index in skipped:
+                continue
+            if manager is not None and index >= boundary:
+                at = position[index]
+                tokens = manager.block(
+                    index, tokens, cond,
+                    forward_prefetch=streamed[at + 1] if at + 1 < len(streamed) else None,
+                    backward_prefetch=streamed[at - 1] if at else None,
+                    checkpoint_block=torch.is_grad_enabled(),
+                )
+            elif index >= boundary:
+                tokens = offloaded_block(layer, tokens, cond)
+            elif self.gradient_checkpointing and self.training and torch.is_grad_enabled():
+                tokens = checkpoint(layer, tokens, cond, use_reentrant=False)
+            else:
+                tokens = layer(tokens, cond)
+        return tokens
 
 
 def inject_lora(model: nn.Module, rank: int, alpha: float, targets: tuple[str, ...] = ("q", "k", "v", "o"),

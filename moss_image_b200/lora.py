@@ -119,6 +119,7 @@ class LoRALinear(nn.Module):
         base = self.base
         if (
             isinstance(base, FrozenInt8Linear)
+            and base.fuses_lora
             and tokens.device.type == "cuda"
             and adapter_dtype in (torch.float16, torch.bfloat16)
             and autocast_compute_dtype(tokens, base.compute_dtype) == adapter_dtype

@@ -71,6 +71,10 @@ class FrozenInt8Linear(nn.Module):
     allocates a transient decoded tensor; call the module for computation.
     """
 
+    # The module multiplies its input by dec(weight_int8)^T unchanged, so an adapter's
+    # update can share its GEMM (subclasses that transform the input set this to False).
+    fuses_lora = True
+
     def __init__(self, linear: nn.Linear, *, backend: str = "eager") -> None:
         super().__init__()
         if linear.weight.requires_grad or (linear.bias is not None and linear.bias.requires_grad):

@@ -138,3 +138,24 @@ def test_large_rotation_and_gemm_shapes(cuda_device):
     q, s = module.weight_int8.cpu().numpy(), module.weight_scale.cpu().numpy()
     expected = O.gemm_fwd(O.hadamard(_np(x), 256, O.BF16), q, s, w_kind=O.BF16, v_kind=O.BF16)
     assert O.rel_fro(_np(y), expected) <= REL_FRO_TOL
+
+
+def test_lora_over_a_convrot_base_adds_the_update_to_the_rotated_product(cuda_device):
+    """A LoRA adapter wrapping a ConvRot layer (the reference injects LoRA before quantising)
+    sees the unrotated input: y = (x H) dec(W H)^T + scale (x A^T) B^T."""
+    from moss_image_b200.lora import LoRALinear
+
+    torch.manual_seed(21)
+    base = nn.Linear(512, 192, bias=True).requires_grad_(False).to(cuda_device)
+    lora = LoRALinear(base, 8, 16.0)
+    with torch.no_grad():
+        lora.lora_B.normal_(0.0, 0.05)
+    lora.base = FrozenConvRotLinear(base, 128)
+    lora = lora.to(cuda_device, torch.bfloat16)
+    x = torch.randn(3, 40, 512, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = lora(x)
+    y.float().square().sum().backward()
+    expected = lora.base(x.detach()).float() + lora.scale * (x.detach().float() @ lora.lora_A.float().t()) @ lora.lora_B.float().t()
+    assert O.rel_fro(_np(y), expected.cpu().numpy()) <= 1e-2
+    assert lora.lora_A.grad is not None and torch.isfinite(lora.lora_A.grad).all()
