@@ -56,7 +56,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
     p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx"], default=None)
+    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load"],
+                   default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
     p.add_argument("--m", type=int, default=9216)
     p.add_argument("--k", type=int, default=3072)
@@ -257,10 +258,68 @@ def run_reference(args: argparse.Namespace) -> None:
 
 
 # ----------------------------------------------------------------------------- kernel-only modes
+def run_comfy_load(args: argparse.Namespace) -> None:
+    """Load one block's worth of Comfy int8_tensorwise linears: dense decode + re-quantise
+    (what a decode-only loader leads to) against keeping the stored codes."""
+    import torch
+
+    from moss_image_b200.comfy_weights import decode_comfy_state, split_comfy_state
+    from moss_image_b200.quantization import FrozenInt8Linear
+
+    dev = torch.device("cuda", 0)
+    shapes = {"q": (DIM, DIM), "k": (DIM, DIM), "v": (DIM, DIM), "o": (DIM, DIM), "up": (MLP, DIM),
+              "down": (DIM, MLP), "adaln": (6 * DIM, DIM)}
+    gen = torch.Generator().manual_seed(0)
+    marker = torch.tensor(list(b'{"format": "int8_tensorwise"}'), dtype=torch.uint8)
+    state = {}
+    for name, (n, k) in shapes.items():
+        state[f"{name}.weight"] = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+        state[f"{name}.weight_scale"] = (torch.rand(n, 1, generator=gen) * 2e-4 + 1e-4).float()
+        state[f"{name}.comfy_quant"] = marker
+    nbytes = sum(n * k for n, k in shapes.values())
+
+    def via_dense():
+        dense = decode_comfy_state(state, torch.bfloat16)
+        out = {}
+        for name in shapes:
+            linear = torch.nn.Linear(1, 1, bias=False)
+            linear.weight = torch.nn.Parameter(dense[f"{name}.weight"].to(dev), requires_grad=False)
+            linear.in_features, linear.out_features = shapes[name][1], shapes[name][0]
+            out[name] = FrozenInt8Linear(linear)
+        torch.cuda.synchronize()
+        return out
+
+    def direct():
+        quantized, _ = split_comfy_state(state)
+        out = {name: FrozenInt8Linear.from_codes(w.codes.to(dev), w.scale.reshape(-1).to(dev))
+               for name, w in quantized.items()}
+        torch.cuda.synchronize()
+        return out
+
+    results = {}
+    for label, fn in (("decode_requantize", via_dense), ("direct", direct)):
+        fn()
+        times = []
+        for _ in range(max(1, args.steps)):
+            t0 = time.perf_counter()
+            modules = fn()
+            times.append(time.perf_counter() - t0)
+        results[label] = {"ms": 1e3 * statistics.median(times)}
+        moved = sum(int((modules[n].weight_int8.cpu() != state[f"{n}.weight"]).sum()) for n in shapes)
+        results[label]["codes_changed_frac"] = moved / nbytes
+    print(json.dumps({"kernel": "comfy_load", "block_linears": len(shapes), "int8_bytes": nbytes,
+                      "threads": torch.get_num_threads(), **results,
+                      "speedup": results["decode_requantize"]["ms"] / results["direct"]["ms"]}), flush=True)
+
+
 def run_kernel(args: argparse.Namespace) -> None:
     import torch
 
     from moss_image_b200 import quant_kernels as qk
+
+    if args.kernel == "comfy_load":
+        run_comfy_load(args)
+        return
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)

@@ -120,6 +120,19 @@ class FrozenConvRotLinear(FrozenInt8Linear):
         self.group_size = group
         self.register_buffer("rotation_group_size", torch.tensor(group, device=linear.weight.device))
 
+    @classmethod
+    def from_codes(cls, codes: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None,
+                   group_size: int = 256, *, dtype: torch.dtype = torch.bfloat16,
+                   backend: str = "eager") -> "FrozenConvRotLinear":
+        """Wrap stored codes of ``W H`` (int8 ``[out, in]``, per-row float32 scales ``[out]``)
+        rotated with ``group_size``, without decoding or re-quantising them."""
+        if effective_group_size(codes.shape[1], group_size) != group_size:
+            raise ValueError("ConvRot group size must be a power of two that divides the input width.")
+        module = super().from_codes(codes, scale, bias, dtype=dtype, backend=backend)
+        module.group_size = group_size
+        module.register_buffer("rotation_group_size", torch.tensor(group_size, device=codes.device))
+        return module
+
     @property
     def weight(self) -> torch.Tensor:
         """Transient decoded weight in the original, unrotated basis."""

@@ -81,16 +81,41 @@ class FrozenInt8Linear(nn.Module):
             raise ValueError("Freeze the base linear before quantizing it (LoRA training only).")
         if linear.weight.device.type == "meta":
             raise ValueError("Load the base weights before quantizing them.")
-        self.in_features = linear.in_features
-        self.out_features = linear.out_features
-        self._quantized_backend = validate_quantized_backend(backend)
+        validate_quantized_backend(backend)
         codes, scale = quantize_weight(linear.weight.detach())
+        bias = None if linear.bias is None else linear.bias.detach().clone()
+        self._set_codes(codes, scale, bias, linear.weight.dtype, backend)
+
+    @classmethod
+    def from_codes(cls, codes: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None, *,
+                   dtype: torch.dtype = torch.bfloat16, backend: str = "eager") -> "FrozenInt8Linear":
+        """Wrap stored codes (int8 ``[out, in]``) and per-row float32 scales (``[out]``) as they
+        are - e.g. a quantised checkpoint's - without decoding or re-quantising them.
+
+        ``dtype`` is the compute dtype (what ``.to(dtype)`` would have set).
+        """
+        if codes.dtype != torch.int8 or codes.ndim != 2:
+            raise ValueError("int8 codes must be an int8 [out, in] tensor.")
+        if scale.dtype != torch.float32 or tuple(scale.shape) != (codes.shape[0],):
+            raise ValueError("weight scales must be float32 [out].")
+        if scale.device != codes.device or (bias is not None and bias.device != codes.device):
+            raise ValueError("codes, scales and bias must be on one device.")
+        if bias is not None and tuple(bias.shape) != (codes.shape[0],):
+            raise ValueError("bias must be [out].")
+        module = cls.__new__(cls)
+        nn.Module.__init__(module)
+        module._set_codes(codes.contiguous(), scale.contiguous(), bias, dtype, validate_quantized_backend(backend))
+        return module
+
+    def _set_codes(self, codes: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None, dtype: torch.dtype,
+                   backend: str) -> None:
+        self.in_features = codes.shape[1]
+        self.out_features = codes.shape[0]
+        self._quantized_backend = backend
         self.register_buffer("weight_int8", codes)
         self.register_buffer("weight_scale", scale)
-        self.register_buffer(
-            "_dtype_anchor", torch.empty(0, device=linear.weight.device, dtype=linear.weight.dtype), persistent=False
-        )
-        self.register_buffer("bias", None if linear.bias is None else linear.bias.detach().clone())
+        self.register_buffer("_dtype_anchor", torch.empty(0, device=codes.device, dtype=dtype), persistent=False)
+        self.register_buffer("bias", bias)
 
     @property
     def compute_dtype(self) -> torch.dtype:

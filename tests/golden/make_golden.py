@@ -15,7 +15,11 @@ and records, on CPU:
   sliced layouts (training/tests/test_packed_features.py:201-235 and more);
 * ConvRot (``training.convrot``): ``rotate_hadamard`` outputs in f32 and f64 for every
   group size from 1 to 512, ``effective_group_size`` answers, and the codes, scales,
-  rotated weights, eager outputs and input gradients of ``FrozenConvRotLinear``.
+  rotated weights, eager outputs and input gradients of ``FrozenConvRotLinear``;
+* Comfy ``int8_tensorwise`` storage (``training.comfy_weights``): dense decodes of the seeded
+  cases in ``comfy_cases.py`` (plain and ConvRot, every output dtype), the hash of a decode
+  large enough to run in several row chunks, and the reference's error message for each
+  malformed state.
 
 Outputs: tests/golden/golden.npz (small arrays) and tests/golden/golden.json (hashes and
 metadata). The GPU box never runs this script; the tests read the committed outputs.
@@ -34,6 +38,8 @@ import torch
 from torch import nn
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+from comfy_cases import COMFY_CASES, comfy_codes, comfy_fixture, comfy_marker, comfy_mutations  # noqa: E402
 
 # Weight shapes [out, in] of BASELINE.json configs 1/2/5 (q/k/v/o, MLP up/down, adaLN)
 # and the real MOSS block's fused up-gate and down projections.
@@ -221,6 +227,39 @@ def main() -> None:
         arrays[f"{name}.dx"] = to_np(tokens.grad.float())
         meta["cases"][name] = {"dtype": str(dtype).split(".")[-1], "group": module.group_size,
                                "rotation_group_size": int(module.rotation_group_size.item())}
+
+    # ---------------------------------------------------------------- Comfy int8_tensorwise
+    from training.comfy_weights import decode_comfy_state  # noqa: E402
+
+    meta["comfy"] = {}
+    for name, rows, cols, fields, dtype in COMFY_CASES:
+        codes, scale = comfy_codes(rows, cols, seed=len(meta["comfy"]) + 700)
+        state = {"layer.weight": codes, "layer.weight_scale": scale, "layer.comfy_quant": comfy_marker(fields),
+                 "layer.bias": torch.linspace(-1, 1, rows), "norm.num_batches_tracked": torch.tensor(9)}
+        dense = decode_comfy_state(state, dtype)
+        arrays[f"{name}.codes"] = codes.numpy()
+        arrays[f"{name}.scale"] = scale.numpy()
+        arrays[f"{name}.dense"] = dense["layer.weight"].to(torch.float64).numpy()
+        meta["comfy"][name] = {"fields": fields, "dtype": str(dtype).split(".")[-1],
+                               "keys": sorted(dense), "bias_dtype": str(dense["layer.bias"].dtype).split(".")[-1],
+                               "counter_dtype": str(dense["norm.num_batches_tracked"].dtype).split(".")[-1]}
+    # a table wide enough to be decoded in several row chunks: hashes only
+    codes, scale = comfy_codes(600, 8192, seed=799)
+    fields = {"format": "int8_tensorwise", "convrot": True, "convrot_groupsize": 256}
+    dense = decode_comfy_state({"embed.weight": codes, "embed.weight_scale": scale,
+                                "embed.comfy_quant": comfy_marker(fields)}, torch.bfloat16)["embed.weight"]
+    meta["comfy_chunked"] = {"rows": 600, "cols": 8192, "seed": 799, "fields": fields,
+                             "codes_sha": sha(codes.numpy()), "dense_bf16_sha": sha(dense.view(torch.int16).numpy())}
+    meta["comfy_errors"] = {}
+    for label, mutate in comfy_mutations().items():
+        state = comfy_fixture()
+        mutate(state)
+        try:
+            decode_comfy_state(state)
+        except ValueError as error:
+            meta["comfy_errors"][label] = str(error)
+        else:
+            raise AssertionError(f"reference accepted the malformed case {label}")
 
     np.savez_compressed(HERE / "golden.npz", **arrays)
     (HERE / "golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
