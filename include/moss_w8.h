@@ -179,6 +179,35 @@ MOSS_API int moss_hadamard_rotate(const void* x, int dtype, int64_t rows, int64_
                          moss_stream_t stream);
 
 /*
+ * Per-sequence conditioning of a packed token stream (replaces the index_select expansion
+ * of _modulation_sample_indices/_condition_for_tokens and the elementwise ops that consume
+ * it, training/model.py:288-312,752-771). Rows [offsets[s], offsets[s+1]) of the
+ * [rows, dim] stream belong to sequence s; its condition is row s of scale/shift/gate,
+ * whose rows are cond_stride elements apart (views of a [segments, 6, dim] modulation need
+ * no copy). offsets: device int64 [segments + 1], offsets[0] = 0, offsets[segments] = rows.
+ * The result dtype is x's when cond has the same dtype, else F32 (torch type promotion);
+ * every product and sum is rounded to it in the reference's order (no FMA contraction).
+ *   modulate  y = x * (1 + scale[s]) + shift[s]       (1 + scale rounded to cond dtype)
+ *   gate      y = x + update * gate[s]                (update has x's dtype)
+ * The backward entry points write the gradient of x (modulate) or of update (gate),
+ * rounded like the reference's autograd, and, when dscale/dshift/dgate are non-null, ADD
+ * the per-sequence condition gradients into those f32 [segments, dim] arrays (summed in f32;
+ * the caller zeroes them and rounds to the condition dtype).
+ */
+MOSS_API int moss_segment_modulate(const void* x, int x_dtype, int64_t rows, int64_t dim, const void* scale,
+                          const void* shift, int cond_dtype, int64_t cond_stride, const int64_t* offsets,
+                          int64_t segments, void* y, moss_stream_t stream);
+MOSS_API int moss_segment_modulate_bwd(const void* dy, const void* x, int x_dtype, int64_t rows, int64_t dim,
+                              const void* scale, int cond_dtype, int64_t cond_stride, const int64_t* offsets,
+                              int64_t segments, void* dx, float* dscale, float* dshift, moss_stream_t stream);
+MOSS_API int moss_segment_gate(const void* x, const void* update, int x_dtype, int64_t rows, int64_t dim,
+                      const void* gate, int cond_dtype, int64_t cond_stride, const int64_t* offsets,
+                      int64_t segments, void* y, moss_stream_t stream);
+MOSS_API int moss_segment_gate_bwd(const void* dy, const void* update, int x_dtype, int64_t rows, int64_t dim,
+                          const void* gate, int cond_dtype, int64_t cond_stride, const int64_t* offsets,
+                          int64_t segments, void* dupdate, float* dgate, moss_stream_t stream);
+
+/*
  * Dense gather of a strided (non-overlapping) view into a contiguous buffer, and the
  * inverse scatter. Used by the activation offload to turn the payload views of
  * _offload_view (training/activation_offload.py:32-61) into one copy-engine transfer and

@@ -57,6 +57,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _sz, _vp, _vp],
     ),
     "moss_hadamard_rotate": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp]),
+    "moss_segment_modulate": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
+    "moss_segment_modulate_bwd": (
+        _i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "moss_segment_gate": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
+    "moss_segment_gate_bwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp]),
     "moss_strided_gather": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "moss_strided_scatter": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "moss_offload_ring_create": (_i32, [_i32, _sz, _sz, _vp, _vp, ctypes.POINTER(_vp)]),

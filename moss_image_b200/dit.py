@@ -26,6 +26,17 @@ from torch.utils.checkpoint import checkpoint
 from .activation_offload import activation_cpu_offload
 from .lora import LoRALinear
 from .memory import offloaded_block
+from .packed import (
+    CHECKPOINT_CHECK,
+    batch_offsets,
+    condition_for_tokens,
+    cumulative_lengths,
+    modulation_sample_indices,
+    segment_gate,
+    segment_modulate,
+    sequence_max_length,
+    varlen_attention,
+)
 from .quantization import quantize_frozen_linears
 
 
@@ -64,21 +75,50 @@ class SyntheticBlock(nn.Module):
         self.mlp_down = nn.Linear(mlp_dim, dim, bias=True)
         self.adaln = nn.Linear(dim, 6 * dim, bias=True)
 
-    def forward(self, tokens: torch.Tensor, cond: torch.Tensor) -> torch.Tensor:
-        """tokens: [B, T, dim]; cond: [B, dim] (timestep embedding)."""
+    def forward(self, tokens: torch.Tensor, cond: torch.Tensor, cu_seqlens: torch.Tensor | None = None) -> torch.Tensor:
+        """tokens: [B, T, dim] with cond [B, dim] (timestep embedding per sample), or a packed
+        [1, total, dim] stream with cu_seqlens (int64 [S + 1]) and cond [S, dim].
+
+        The conditioning follows training/model.py:288-312: ``norm(x) * (1 + scale) + shift``
+        and ``x + branch * gate`` per sample, each op rounded in the activation dtype. On CUDA
+        the per-sample conditions are applied by the native segment kernels; attention is
+        block-diagonal over the packed sequences.
+        """
         batch, seq, dim = tokens.shape
-        modulation = self.adaln(F.silu(cond)).view(batch, 6, dim)
-        shift_a, scale_a, gate_a, shift_f, scale_f, gate_f = (m.unsqueeze(1) for m in modulation.unbind(1))
-        # modulation and gated residuals as single fused multiply-adds
-        h = torch.addcmul(shift_a, self.norm1(tokens), 1 + scale_a)
+        sequences = cond.shape[0]
+        modulation = self.adaln(F.silu(cond)).view(sequences, 6, dim)
+        shift_a, scale_a, gate_a, shift_f, scale_f, gate_f = modulation.unbind(1)
+        if cu_seqlens is None:
+            offsets, max_length = batch_offsets(batch, seq, tokens.device), seq
+        else:
+            offsets, max_length = cu_seqlens, sequence_max_length(cu_seqlens)
+        if tokens.is_cuda:
+            def modulate(x, scale, shift):
+                return segment_modulate(x, scale, shift, offsets)
+
+            def gated(x, branch, gate):
+                return segment_gate(x, branch, gate, offsets)
+        else:  # the reference's expansion (training/model.py:752-772)
+            index = modulation_sample_indices(modulation, tokens, cu_seqlens)
+
+            def modulate(x, scale, shift):
+                return x * (1 + condition_for_tokens(scale, index)) + condition_for_tokens(shift, index)
+
+            def gated(x, branch, gate):
+                return x + branch * condition_for_tokens(gate, index)
+
+        h = modulate(self.norm1(tokens), scale_a, shift_a)
         q = self.q_norm(self.proj["q"](h).unflatten(-1, (self.heads, -1)))
         k = self.k_norm(self.proj["k"](h).unflatten(-1, (self.heads, -1)))
         v = self.proj["v"](h).unflatten(-1, (self.heads, -1))
-        attended = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
-        attended = attended.transpose(1, 2).flatten(2)
-        tokens = torch.addcmul(tokens, self.proj["o"](attended), gate_a)
-        h = torch.addcmul(shift_f, self.norm2(tokens), 1 + scale_f)
-        return torch.addcmul(tokens, self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")), gate_f)
+        if cu_seqlens is None:
+            attended = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+            attended = attended.transpose(1, 2).flatten(2)
+        else:
+            attended = varlen_attention(q[0], k[0], v[0], offsets, max_length).flatten(1).unsqueeze(0)
+        tokens = gated(tokens, self.proj["o"](attended), gate_a)
+        h = modulate(self.norm2(tokens), scale_f, shift_f)
+        return gated(tokens, self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")), gate_f)
 
 
 class TimestepEmbedding(nn.Module):
@@ -115,7 +155,31 @@ class SyntheticDiT(nn.Module):
             tokens = self._run_layers(tokens, cond, frozenset(skip_layers))
             return self.final_norm(tokens)
 
-    def _run_layers(self, tokens: torch.Tensor, cond: torch.Tensor, skipped: frozenset[int]) -> torch.Tensor:
+    def forward_packed(self, samples: list[torch.Tensor], timestep: torch.Tensor) -> list[torch.Tensor]:
+        """One traversal over a heterogeneous batch: ``samples[i]`` is ``[tokens_i, dim]``.
+
+        Mirrors ``forward_packed`` (training/model.py:502-626): the samples are concatenated
+        into one ``[1, total, dim]`` stream with cumulative boundaries, every linear runs once
+        over all tokens, attention is isolated per sample, and each sample keeps its own
+        timestep conditioning. Returns the per-sample outputs.
+        """
+        if not samples:
+            raise ValueError("forward_packed requires at least one sample.")
+        device = samples[0].device
+        if any(sample.ndim != 2 or sample.shape[0] == 0 or sample.device != device for sample in samples):
+            raise ValueError("Each packed sample must be a non-empty [tokens, dim] tensor on one device.")
+        lengths = [sample.shape[0] for sample in samples]
+        times = torch.as_tensor(timestep, device=device).reshape(-1).expand(len(samples))
+        cu_seqlens = cumulative_lengths(lengths, device)
+        cu_seqlens.moss_max_length = max(lengths)  # known on the host: no device read per block
+        tokens = torch.cat(samples, 0).unsqueeze(0)
+        with activation_cpu_offload(self, self.activation_offload, device):
+            cond = self.time_embedding(times).to(tokens.dtype)
+            tokens = self._run_layers(tokens, cond, frozenset(), cu_seqlens)
+            return list(self.final_norm(tokens)[0].split(lengths, 0))
+
+    def _run_layers(self, tokens: torch.Tensor, cond: torch.Tensor, skipped: frozenset[int],
+                    cu_seqlens: torch.Tensor | None = None) -> torch.Tensor:
         """Resident, synchronously swapped or streamed blocks, as ``place_model`` left them.
 
         Mirrors training/model.py:672-709: blocks at or past ``len(layers) - blocks_to_swap``
@@ -130,20 +194,21 @@ class SyntheticDiT(nn.Module):
         for index, layer in enumerate(self.layers):
             if index in skipped:
                 continue
+            inputs = (tokens, cond) if cu_seqlens is None else (tokens, cond, cu_seqlens)
             if manager is not None and index >= boundary:
                 at = position[index]
                 tokens = manager.block(
-                    index, tokens, cond,
+                    index, *inputs,
                     forward_prefetch=streamed[at + 1] if at + 1 < len(streamed) else None,
                     backward_prefetch=streamed[at - 1] if at else None,
                     checkpoint_block=torch.is_grad_enabled(),
                 )
             elif index >= boundary:
-                tokens = offloaded_block(layer, tokens, cond)
+                tokens = offloaded_block(layer, *inputs)
             elif self.gradient_checkpointing and self.training and torch.is_grad_enabled():
-                tokens = checkpoint(layer, tokens, cond, use_reentrant=False)
+                tokens = checkpoint(layer, *inputs, use_reentrant=False, determinism_check=CHECKPOINT_CHECK)
             else:
-                tokens = layer(tokens, cond)
+                tokens = layer(*inputs)
         return tokens
 
 
@@ -204,6 +269,23 @@ def build_lora_model(depth: int, *, device: torch.device, dim: int = 3072, heads
         layers.append(block)
     model.layers = nn.ModuleList(layers)
     return model
+
+
+def packed_flow_matching_loss(model: SyntheticDiT, latents: list[torch.Tensor], text: list[torch.Tensor],
+                              t: torch.Tensor, noise: list[torch.Tensor]) -> torch.Tensor:
+    """The flow-matching loss of a heterogeneous batch in one packed traversal.
+
+    ``latents[i]``/``noise[i]``: ``[image_tokens_i, dim]``; ``text[i]``: ``[text_tokens_i, dim]``.
+    Each sample's loss is its mean over its image tokens; the batch loss is their mean.
+    """
+    samples = []
+    for latent, context, noise_i, sigma in zip(latents, text, noise, t):
+        sigma = sigma.to(latent.dtype)
+        samples.append(torch.cat(((1 - sigma) * latent + sigma * noise_i, context), 0))
+    outputs = model.forward_packed(samples, t)
+    losses = [F.mse_loss(out[: latent.shape[0]].float(), (noise_i - latent).float())
+              for out, latent, noise_i in zip(outputs, latents, noise)]
+    return torch.stack(losses).mean()
 
 
 def flow_matching_loss(model: SyntheticDiT, latents: torch.Tensor, text: torch.Tensor, t: torch.Tensor,

@@ -33,6 +33,7 @@ from torch.func import functional_call
 from torch.utils.checkpoint import checkpoint
 
 from . import _lib
+from .packed import CHECKPOINT_CHECK
 
 NUM_STAGING_SLOTS = 2
 _ALIGNMENT = 256
@@ -54,7 +55,7 @@ def offloaded_block(layer: nn.Module, *args: torch.Tensor) -> torch.Tensor:
         return functional_call(layer, values, inputs[len(names):], strict=True)
 
     if torch.is_grad_enabled():
-        return checkpoint(run, *parameters, *args, use_reentrant=False)
+        return checkpoint(run, *parameters, *args, use_reentrant=False, determinism_check=CHECKPOINT_CHECK)
     return run(*parameters, *args)
 
 
@@ -383,6 +384,7 @@ class AsyncBlockStreamer:
             return self._run(index, arguments[:count], adapters, completion, forward_prefetch, backward_prefetch)
 
         return checkpoint(run, *input_aliases, *adapter_aliases, use_reentrant=False,
+                          determinism_check=CHECKPOINT_CHECK,
                           context_fn=self._checkpoint_contexts)
 
     def close(self) -> None:
