@@ -278,6 +278,12 @@ def _int64_array(values) -> ctypes.Array:
     return (ctypes.c_int64 * max(1, len(values)))(*values)
 
 
+# Attribute that keeps a saved tensor resident. Packed batches set it on their sequence
+# boundaries: the boundaries are tiny, and a jagged attention recomputed under a checkpoint
+# must see the same boundaries tensor the forward saw.
+KEEP_RESIDENT = "moss_keep_resident"
+
+
 def activation_cpu_offload(
     model: nn.Module,
     enabled: bool,
@@ -316,7 +322,7 @@ def activation_cpu_offload(
     scope = _OffloadScope(offload_ring(scope_device), prefetch_bytes)
 
     def pack(tensor: torch.Tensor):
-        if tensor.device.type != "cuda" or is_weight_backed(tensor):
+        if tensor.device.type != "cuda" or is_weight_backed(tensor) or getattr(tensor, KEEP_RESIDENT, False):
             return tensor
         view = _offload_view(tensor)
         if view is None:

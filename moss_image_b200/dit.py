@@ -10,8 +10,12 @@ residual, modulated MLP with a gated residual. Every linear is a
 
 The stack wraps its forward in :func:`activation_cpu_offload` and checkpoints each block
 (non-reentrant), as the reference trainer does with ``grad_checkpointing: true``
-(training/model.py:687-709), so the offloaded tensors are the block inputs.
-Attention uses torch's scaled-dot-product attention (library code; not part of this path).
+(training/model.py:687-709), so the offloaded tensors are the block inputs. Blocks may be
+swapped or streamed with :func:`~moss_image_b200.memory.place_model`, and
+:meth:`SyntheticDiT.forward_packed` runs a heterogeneous batch as one packed stream.
+Per-sample modulation and gates are applied by the native segment kernels on CUDA
+(:mod:`moss_image_b200.packed`). Attention uses torch's scaled-dot-product attention (library
+code; the jagged, variable-length form for packed streams).
 """
 
 from __future__ import annotations
@@ -23,7 +27,7 @@ from torch import nn
 from torch.nn import functional as F
 from torch.utils.checkpoint import checkpoint
 
-from .activation_offload import activation_cpu_offload
+from .activation_offload import KEEP_RESIDENT, activation_cpu_offload
 from .lora import LoRALinear
 from .memory import offloaded_block
 from .packed import (
@@ -172,6 +176,7 @@ class SyntheticDiT(nn.Module):
         times = torch.as_tensor(timestep, device=device).reshape(-1).expand(len(samples))
         cu_seqlens = cumulative_lengths(lengths, device)
         cu_seqlens.moss_max_length = max(lengths)  # known on the host: no device read per block
+        setattr(cu_seqlens, KEEP_RESIDENT, True)  # the same boundaries tensor in every recomputation
         tokens = torch.cat(samples, 0).unsqueeze(0)
         with activation_cpu_offload(self, self.activation_offload, device):
             cond = self.time_embedding(times).to(tokens.dtype)
