@@ -58,8 +58,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
     p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load"],
-                   default=None)
+    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load",
+                                        "segment_modulate", "segment_gate"], default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
     p.add_argument("--m", type=int, default=9216)
     p.add_argument("--k", type=int, default=3072)
@@ -344,6 +344,17 @@ def run_kernel(args: argparse.Namespace) -> None:
         dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.convrot_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16,  # noqa: E731
                                          args.group)
+    elif args.kernel in ("segment_modulate", "segment_gate"):
+        from moss_image_b200 import packed
+
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        u = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
+        modulation = torch.randn(2, 6, k, device=dev, generator=gen).to(torch.bfloat16)
+        offsets = packed.cumulative_lengths([m // 2, m - m // 2], dev)
+        if args.kernel == "segment_modulate":
+            fn = lambda: packed.segment_modulate(x, modulation[:, 1], modulation[:, 0], offsets)  # noqa: E731
+        else:
+            fn = lambda: packed.segment_gate(x, u, modulation[:, 2], offsets)  # noqa: E731
     else:
         dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)  # noqa: E731
@@ -362,6 +373,9 @@ def run_kernel(args: argparse.Namespace) -> None:
     if args.kernel == "hadamard":
         line["gbs"] = 2.0 * m * k * 2 / ms / 1e6  # one bf16 read and one write
         line["group"] = args.group
+    elif args.kernel.startswith("segment_"):
+        streams = 2 if args.kernel == "segment_modulate" else 3  # bf16 rows read + written
+        line["gbs"] = streams * m * k * 2 / ms / 1e6
     else:
         line["tflops"] = 2.0 * m * n * k / ms / 1e9
     print(json.dumps(line), flush=True)

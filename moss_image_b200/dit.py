@@ -38,7 +38,7 @@ from .packed import (
     modulation_sample_indices,
     segment_gate,
     segment_modulate,
-    sequence_max_length,
+    sequence_lengths,
     varlen_attention,
 )
 from .quantization import quantize_frozen_linears
@@ -92,10 +92,7 @@ class SyntheticBlock(nn.Module):
         sequences = cond.shape[0]
         modulation = self.adaln(F.silu(cond)).view(sequences, 6, dim)
         shift_a, scale_a, gate_a, shift_f, scale_f, gate_f = modulation.unbind(1)
-        if cu_seqlens is None:
-            offsets, max_length = batch_offsets(batch, seq, tokens.device), seq
-        else:
-            offsets, max_length = cu_seqlens, sequence_max_length(cu_seqlens)
+        offsets = batch_offsets(batch, seq, tokens.device) if cu_seqlens is None else cu_seqlens
         if tokens.is_cuda:
             def modulate(x, scale, shift):
                 return segment_modulate(x, scale, shift, offsets)
@@ -119,7 +116,7 @@ class SyntheticBlock(nn.Module):
             attended = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
             attended = attended.transpose(1, 2).flatten(2)
         else:
-            attended = varlen_attention(q[0], k[0], v[0], offsets, max_length).flatten(1).unsqueeze(0)
+            attended = varlen_attention(q[0], k[0], v[0], offsets, sequence_lengths(cu_seqlens)).flatten(1)[None]
         tokens = gated(tokens, self.proj["o"](attended), gate_a)
         h = modulate(self.norm2(tokens), scale_f, shift_f)
         return gated(tokens, self.mlp_down(F.gelu(self.mlp_up(h), approximate="tanh")), gate_f)
@@ -175,7 +172,7 @@ class SyntheticDiT(nn.Module):
         lengths = [sample.shape[0] for sample in samples]
         times = torch.as_tensor(timestep, device=device).reshape(-1).expand(len(samples))
         cu_seqlens = cumulative_lengths(lengths, device)
-        cu_seqlens.moss_max_length = max(lengths)  # known on the host: no device read per block
+        cu_seqlens.moss_lengths = tuple(lengths)  # known on the host: no device read per block
         setattr(cu_seqlens, KEEP_RESIDENT, True)  # the same boundaries tensor in every recomputation
         tokens = torch.cat(samples, 0).unsqueeze(0)
         with activation_cpu_offload(self, self.activation_offload, device):

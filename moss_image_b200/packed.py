@@ -37,6 +37,8 @@ _ATTENTION_BACKENDS = {"auto", "sdpa", "sdpa_cudnn", "flash_attn_2"}
 # Checkpoint recomputation check for blocks that run variable-length attention: the default
 # check reads the shape of every saved tensor, which jagged (nested) tensors do not have.
 CHECKPOINT_CHECK = "none"
+# Packed streams with at most this many sequences run one dense attention call per sequence.
+VARLEN_LOOP_MAX_SEQUENCES = 32
 _JAGGED_BACKENDS = [torch.nn.attention.SDPBackend.FLASH_ATTENTION, torch.nn.attention.SDPBackend.EFFICIENT_ATTENTION,
                     torch.nn.attention.SDPBackend.MATH]
 
@@ -110,17 +112,25 @@ def scaled_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor
 
 
 def varlen_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, offsets: torch.Tensor,
-                     max_length: int) -> torch.Tensor:
+                     lengths: tuple[int, ...]) -> torch.Tensor:
     """Block-diagonal attention over packed ``[total, heads, head_dim]`` rows.
 
-    ``offsets`` holds the int64 sequence boundaries on the tensors' device; each sequence
-    attends only to itself. The rows must be contiguous ``[total, heads, head_dim]``. Runs torch's jagged SDPA (a variable-length flash kernel on CUDA):
-    memory is linear in ``total``.
+    ``offsets`` holds the int64 sequence boundaries on the tensors' device and ``lengths`` the
+    same boundaries on the host; each sequence attends only to itself, and memory stays linear
+    in ``total``. The rows must be contiguous. Up to ``VARLEN_LOOP_MAX_SEQUENCES`` sequences
+    run one dense attention call per sequence on views of the packed rows (cuDNN's Blackwell
+    kernels; the split's backward writes the packed gradient once). More sequences run torch's
+    jagged attention (a variable-length flash kernel) in one call.
     """
+    if len(lengths) <= VARLEN_LOOP_MAX_SEQUENCES:
+        parts = [F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                v.transpose(0, 1)[None])[0].transpose(0, 1)
+                 for q, k, v in zip(query.split(lengths), key.split(lengths), value.split(lengths))]
+        return torch.cat(parts, 0)
     from torch.nn.attention import sdpa_kernel
 
     def jagged(tensor: torch.Tensor) -> torch.Tensor:
-        return torch.nested.nested_tensor_from_jagged(tensor, offsets=offsets, max_seqlen=max_length).transpose(1, 2)
+        return torch.nested.nested_tensor_from_jagged(tensor, offsets=offsets, max_seqlen=max(lengths)).transpose(1, 2)
 
     # jagged inputs run on the variable-length flash or memory-efficient kernels (math only
     # for what neither supports); cuDNN has no jagged form
@@ -160,7 +170,7 @@ def scaled_attention_varlen(query: torch.Tensor, key: torch.Tensor, value: torch
             "use 'sdpa' or 'flash_attn_2' for packed batching.")
     offsets = cu_seqlens.to(device=value.device, dtype=torch.int64)
     rows = [t.squeeze(0).transpose(0, 1).contiguous() for t in (query, key, value)]
-    output = varlen_attention(*rows, offsets, max_length)
+    output = varlen_attention(*rows, offsets, tuple(int(n) for n in lengths.tolist()))
     return output.transpose(0, 1).unsqueeze(0)
 
 
@@ -189,13 +199,13 @@ def condition_for_tokens(condition: torch.Tensor, sample_indices: torch.Tensor |
     return condition.index_select(0, sample_indices).unsqueeze(0)
 
 
-def sequence_max_length(cu_seqlens: torch.Tensor) -> int:
-    """Longest sequence of ``cu_seqlens``; read from the device once per boundaries tensor
-    (a packing caller that knows it on the host sets ``cu_seqlens.moss_max_length``)."""
-    known = getattr(cu_seqlens, "moss_max_length", None)
+def sequence_lengths(cu_seqlens: torch.Tensor) -> tuple[int, ...]:
+    """Sequence lengths of ``cu_seqlens`` on the host: read from the device once per boundaries
+    tensor (a packing caller that knows them sets ``cu_seqlens.moss_lengths``)."""
+    known = getattr(cu_seqlens, "moss_lengths", None)
     if known is None:
-        known = int((cu_seqlens[1:] - cu_seqlens[:-1]).max())
-        cu_seqlens.moss_max_length = known
+        known = tuple(int(n) for n in (cu_seqlens[1:] - cu_seqlens[:-1]).tolist())
+        cu_seqlens.moss_lengths = known
     return known
 
 

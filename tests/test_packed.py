@@ -34,6 +34,21 @@ def test_varlen_sdpa_isolates_examples():
     torch.testing.assert_close(actual, expected, rtol=1e-6, atol=1e-6)
 
 
+def test_many_sequences_use_one_jagged_call_with_the_same_result():
+    torch.manual_seed(6)
+    lengths = tuple(int(n) for n in torch.randint(1, 9, (packed.VARLEN_LOOP_MAX_SEQUENCES + 8,)))
+    total = sum(lengths)
+    q, k, v = (torch.randn(total, 2, 8, requires_grad=True) for _ in range(3))
+    offsets = cumulative_lengths(list(lengths), torch.device("cpu"))
+    jagged = packed.varlen_attention(q, k, v, offsets, lengths)
+    looped = torch.cat([F.scaled_dot_product_attention(a.transpose(0, 1)[None], b.transpose(0, 1)[None],
+                                                       c.transpose(0, 1)[None])[0].transpose(0, 1)
+                        for a, b, c in zip(q.split(lengths), k.split(lengths), v.split(lengths))])
+    torch.testing.assert_close(jagged, looped, rtol=1e-6, atol=1e-6)
+    jagged.square().sum().backward()
+    assert torch.isfinite(q.grad).all()
+
+
 def test_varlen_gradients_stay_inside_each_sequence():
     torch.manual_seed(5)
     query, key, value = (torch.randn(1, 2, 9, 8, requires_grad=True) for _ in range(3))
