@@ -591,38 +591,45 @@ SkinnyPlan plan_skinny(int64_t M, int64_t Nc, int64_t Kr, int sms) {
   using namespace skinny;
   SkinnyPlan p;
   if (M <= 0 || Nc <= 0 || Kr <= 0 || M > INT32_MAX) return p;
-  p.nt = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
-  const int64_t tiles_m = (M + p.nt - 1) / p.nt;
   const int64_t tiles_n = (Nc + BM - 1) / BM;
-  const int64_t tiles = tiles_m * tiles_n;
   const int64_t main_kb = (Kr + BK - 1) / BK;
-  if (tiles > INT32_MAX / 64) return p;
-  p.usable = true;
-  p.tiles_m = static_cast<int>(tiles_m);
-  p.tiles_n = static_cast<int>(tiles_n);
-  p.splits = 1;
-  p.kb_per_split = static_cast<int>(main_kb);
-  // Split K when it pays: a rough per-CTA time model in microseconds, per k-block (converter
-  // bound for narrow token tiles, MMA bound for 256) plus a fixed pipeline fill per wave of
-  // units, against the partials a split writes and the reduction kernel reads back.
-  const double t_kb = std::max(0.2, 0.27 * p.nt / 256.0);
-  auto waves = [&](int64_t units) { return static_cast<double>((units + sms - 1) / sms); };
-  double best = waves(tiles) * (main_kb * t_kb + 2.0);
-  const int64_t max_splits = std::min<int64_t>((main_kb + kSub - 1) / kSub, 64);
-  for (int64_t want = 2; want <= max_splits; ++want) {
-    int64_t kps = (main_kb + want - 1) / want;
-    kps = (kps + kSub - 1) / kSub * kSub;
-    const int64_t splits = (main_kb + kps - 1) / kps;
-    if (splits != want) continue;
-    const double cost = waves(tiles * splits) * (kps * t_kb + 2.0) + 2.0 +
-                        2.0 * static_cast<double>(splits) * M * Nc * 4.0 / 5.0e6;
-    if (cost < best) {
-      best = cost;
-      p.splits = static_cast<int>(splits);
-      p.kb_per_split = static_cast<int>(kps);
+  if (((M + 15) / 16) * tiles_n > INT32_MAX / 64) return p;
+  // Token tile and K split from a time model fitted to B200 measurements of this kernel (both
+  // directions, 3072-18432 wide weights, 16-1024 tokens, single launches on a cold L2; median
+  // error 2-3%): each wave of CTAs costs kb x 0.43 us per k-block for token tiles up to 128
+  // (0.66 us at 256, whose MMA takes longer than the conversion), and a split adds ~4 us
+  // for the reduction launch plus its f32 partials written and read back at ~5.5 TB/s.
+  // Everything else (launch, pipeline fill, the cold weight stream) is the same for every
+  // choice and left out.
+  double best = -1.0;
+  for (int nt : {16, 32, 64, 128, 256}) {
+    if (nt > 16 && nt / 2 >= M) continue;  // a tile at least twice the token count buys nothing
+    const double t_kb = nt == 256 ? 0.66 : 0.43;
+    const int64_t tiles = ((M + nt - 1) / nt) * tiles_n;
+    const int64_t max_splits = std::min<int64_t>((main_kb + kSub - 1) / kSub, 64);
+    for (int64_t want = 1; want <= std::max<int64_t>(max_splits, 1); ++want) {
+      int64_t kps = main_kb, splits = 1;
+      if (want > 1) {
+        kps = (main_kb + want - 1) / want;
+        kps = (kps + kSub - 1) / kSub * kSub;
+        splits = (main_kb + kps - 1) / kps;
+        if (splits != want) continue;
+      }
+      const int64_t waves = (tiles * splits + sms - 1) / sms;
+      double cost = static_cast<double>(waves * kps) * t_kb;
+      if (splits > 1) cost += 4.0 + 0.18 * 2.0 * static_cast<double>(splits) * M * Nc * 4.0 / 1.0e6;
+      if (best < 0.0 || cost < best - 1e-9) {
+        best = cost;
+        p.nt = nt;
+        p.tiles_m = static_cast<int>((M + nt - 1) / nt);
+        p.splits = static_cast<int>(splits);
+        p.kb_per_split = static_cast<int>(kps);
+      }
     }
   }
-  if (p.splits > 1) p.partial_bytes = (static_cast<size_t>(p.splits) * M * Nc * 4 + 255) / 256 * 256;
+  p.usable = true;
+  p.tiles_n = static_cast<int>(tiles_n);
+  p.partial_bytes = p.splits > 1 ? (static_cast<size_t>(p.splits) * M * Nc * 4 + 255) / 256 * 256 : 0;
   return p;
 }
 
