@@ -562,6 +562,9 @@ def run_train(args: argparse.Namespace) -> None:
     qk.set_launch_observer(timer)
     props = torch.cuda.get_device_properties(dev)
     clocks = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+    from moss_image_b200 import _lib as moss_lib
+
+    counts0 = dict(moss_lib.launch_counts)
     barrier()
     clocks.start()
     timer.active = True
@@ -575,6 +578,7 @@ def run_train(args: argparse.Namespace) -> None:
     clock_info = clocks.stop()
     elapsed_ms = start.elapsed_time(end)
     stats1 = ring.stats()
+    other_launches = {name: count - counts0.get(name, 0) for name, count in moss_lib.launch_counts.items()}
     swap1 = streamer.copy_statistics() if streamer is not None else None
     gemm = timer.summary()
 
@@ -641,8 +645,11 @@ def run_train(args: argparse.Namespace) -> None:
                         "gbs_over_step": offload_bytes / (elapsed_ms * 1e-3) / 1e9,
                         "pinned_bytes": stats1["pinned_bytes"]},
             "clocks": clock_info,
-            "gpu_launches": launches,
-            "gpu_launches_note": "int8 GEMM launches (fwd + dx) of libmoss_w8.so in the timed region",
+            "gpu_launches": launches + sum(other_launches.values()),
+            "gpu_launches_by_kind": {"int8_gemm": launches, **other_launches},
+            "gpu_launches_note": ("libmoss_w8.so kernel launches in the timed region: int8 GEMM calls (fwd + dx; "
+                                  "a split-K call's extra reduction launch is not counted), per-sample "
+                                  "conditioning, offload gather/scatter"),
             "loss_last": losses[-1] if losses else None,
         }
         if streamer is not None:

@@ -94,6 +94,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
 }
 
+# Kernel launches issued through this binding by the ops that do not go through the GEMM
+# launch observer (segment conditioning, offload gather/scatter); benchmarks read the deltas.
+launch_counts: dict[str, int] = {}
+
+
+def count_launch(name: str) -> None:
+    launch_counts[name] = launch_counts.get(name, 0) + 1
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 _load_error: str | None = None

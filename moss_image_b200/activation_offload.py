@@ -270,6 +270,7 @@ class _OffloadScope:
                 target.data_ptr(), compute.cuda_stream,
             )
             _lib.check(rc, "moss_strided_scatter")
+            _lib.count_launch("strided_copy")
             restored = target
         return restored.as_strided(entry.shape, entry.stride)
 
@@ -340,6 +341,7 @@ def activation_cpu_offload(
                 _int64_array(source.stride()), staged.data_ptr(), compute.cuda_stream,
             )
             _lib.check(rc, "moss_strided_gather")
+            _lib.count_launch("strided_copy")
         ticket = ring.pack(staged.data_ptr(), nbytes, compute)
         if ticket is None:  # ring at its limit: keep this tensor resident, like other exclusions
             return tensor

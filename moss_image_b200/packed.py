@@ -256,6 +256,7 @@ class _SegmentModulate(torch.autograd.Function):
             rows.data_ptr(), _lib.dtype_code(rows.dtype), rows.shape[0], rows.shape[1], scale.data_ptr(),
             shift.data_ptr(), _lib.dtype_code(scale.dtype), scale.stride(0), offsets.data_ptr(), scale.shape[0],
             out.data_ptr(), stream), "moss_segment_modulate")
+        _lib.count_launch("segment")
         ctx.save_for_backward(rows, scale, offsets)
         ctx.shape = tokens.shape
         return out.view(*tokens.shape[:-1], tokens.shape[-1])
@@ -273,6 +274,7 @@ class _SegmentModulate(torch.autograd.Function):
             _lib.dtype_code(scale.dtype), scale.stride(0), offsets.data_ptr(), sequences, d_rows.data_ptr(),
             None if d_scale is None else d_scale.data_ptr(), None if d_shift is None else d_shift.data_ptr(),
             _lib.stream_handle(rows.device)), "moss_segment_modulate_bwd")
+        _lib.count_launch("segment")
         return (d_rows.view(ctx.shape), None if d_scale is None else d_scale.to(scale.dtype),
                 None if d_shift is None else d_shift.to(scale.dtype), None)
 
@@ -287,6 +289,7 @@ class _SegmentGate(torch.autograd.Function):
             rows.data_ptr(), branch.data_ptr(), _lib.dtype_code(rows.dtype), rows.shape[0], rows.shape[1],
             gate.data_ptr(), _lib.dtype_code(gate.dtype), gate.stride(0), offsets.data_ptr(), gate.shape[0],
             out.data_ptr(), _lib.stream_handle(tokens.device)), "moss_segment_gate")
+        _lib.count_launch("segment")
         ctx.save_for_backward(branch, gate, offsets)
         ctx.shape = tokens.shape
         ctx.token_dtype = tokens.dtype
@@ -307,6 +310,7 @@ class _SegmentGate(torch.autograd.Function):
                 gate.data_ptr(), _lib.dtype_code(gate.dtype), gate.stride(0), offsets.data_ptr(), gate.shape[0],
                 d_branch.data_ptr(), None if d_gate is None else d_gate.data_ptr(),
                 _lib.stream_handle(branch.device)), "moss_segment_gate_bwd")
+            _lib.count_launch("segment")
             d_branch = d_branch.view(ctx.shape) if ctx.needs_input_grad[1] else None
             d_gate = None if d_gate is None else d_gate.to(gate.dtype)
         return d_tokens, d_branch, d_gate, None
