@@ -59,7 +59,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load",
-                                        "segment_modulate", "segment_gate"], default=None)
+                                        "segment_modulate", "segment_gate", "rmsnorm", "rmsnorm_bwd"], default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
     p.add_argument("--m", type=int, default=9216)
     p.add_argument("--k", type=int, default=3072)
@@ -344,6 +344,17 @@ def run_kernel(args: argparse.Namespace) -> None:
         dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.convrot_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16,  # noqa: E731
                                          args.group)
+    elif args.kernel in ("rmsnorm", "rmsnorm_bwd"):
+        from moss_image_b200.norms import rms_norm
+
+        x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(args.kernel == "rmsnorm_bwd")
+        wn = torch.ones(k, device=dev, dtype=torch.bfloat16)
+        if args.kernel == "rmsnorm":
+            fn = lambda: rms_norm(x, wn)  # noqa: E731
+        else:
+            yn = rms_norm(x, wn)
+            dyn = torch.randn_like(yn)
+            fn = lambda: torch.autograd.grad(yn, x, dyn, retain_graph=True)  # noqa: E731
     elif args.kernel in ("segment_modulate", "segment_gate"):
         from moss_image_b200 import packed
 
@@ -373,8 +384,9 @@ def run_kernel(args: argparse.Namespace) -> None:
     if args.kernel == "hadamard":
         line["gbs"] = 2.0 * m * k * 2 / ms / 1e6  # one bf16 read and one write
         line["group"] = args.group
-    elif args.kernel.startswith("segment_"):
-        streams = 2 if args.kernel == "segment_modulate" else 3  # bf16 rows read + written
+    elif args.kernel.startswith("segment_") or args.kernel.startswith("rmsnorm"):
+        # bf16 rows read + written: modulate and norm forward 2, gate and norm backward 3
+        streams = 2 if args.kernel in ("segment_modulate", "rmsnorm") else 3
         line["gbs"] = streams * m * k * 2 / ms / 1e6
     else:
         line["tflops"] = 2.0 * m * n * k / ms / 1e9

@@ -208,6 +208,21 @@ MOSS_API int moss_segment_gate_bwd(const void* dy, const void* update, int x_dty
                           int64_t segments, void* dupdate, float* dgate, moss_stream_t stream);
 
 /*
+ * RMSNorm over the last dimension of x [rows, dim] (contiguous) with the reference's
+ * rounding points (RMSNorm.forward, training/model.py:161-172): statistics in f32,
+ *   n = round_x(x * rsqrt(mean(x^2) + eps)),   y = round_y(n * w),
+ * y's dtype = x's if w has it, else F32. rstd (optional, f32 [rows]) receives the per-row
+ * rsqrt for the backward. The backward writes dx (x's dtype) for a frozen w:
+ *   dn = round_x(round_y(dy * w)),   dx = round_x(r * dn - x * r^3 * sum(dn * x) / dim).
+ * Replaces the per-head q/k norms and the block norms of Block._forward_impl
+ * (training/model.py:290,296-297,303).
+ */
+MOSS_API int moss_rmsnorm_fwd(const void* x, int x_dtype, int64_t rows, int64_t dim, const void* weight, int w_dtype,
+                     float eps, void* y, float* rstd, moss_stream_t stream);
+MOSS_API int moss_rmsnorm_bwd(const void* dy, const void* x, int x_dtype, int64_t rows, int64_t dim,
+                     const void* weight, int w_dtype, const float* rstd, void* dx, moss_stream_t stream);
+
+/*
  * Dense gather of a strided (non-overlapping) view into a contiguous buffer, and the
  * inverse scatter. Used by the activation offload to turn the payload views of
  * _offload_view (training/activation_offload.py:32-61) into one copy-engine transfer and

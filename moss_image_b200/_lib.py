@@ -62,6 +62,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
     "moss_segment_gate": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
     "moss_segment_gate_bwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "moss_rmsnorm_fwd": (_i32, [_vp, _i32, _i64, _i64, _vp, _i32, _f32, _vp, _vp, _vp]),
+    "moss_rmsnorm_bwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp, _vp]),
     "moss_strided_gather": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "moss_strided_scatter": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "moss_offload_ring_create": (_i32, [_i32, _sz, _sz, _vp, _vp, ctypes.POINTER(_vp)]),

@@ -30,6 +30,7 @@ from torch.utils.checkpoint import checkpoint
 from .activation_offload import KEEP_RESIDENT, activation_cpu_offload
 from .lora import LoRALinear
 from .memory import offloaded_block
+from .norms import rms_norm
 from .packed import (
     CHECKPOINT_CHECK,
     batch_offsets,
@@ -45,7 +46,9 @@ from .quantization import quantize_frozen_linears
 
 
 class RMSNorm(nn.Module):
-    """Root-mean-square norm with a learned gain (training/model.py RMSNorm semantics)."""
+    """Root-mean-square norm with a learned gain (training/model.py:154-172 arithmetic:
+    f32 statistics, cast to the input dtype, then times the gain). CUDA inputs run the
+    native norm kernels."""
 
     def __init__(self, dim: int, eps: float = 1e-6) -> None:
         super().__init__()
@@ -53,14 +56,10 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda and x.dtype in (torch.float16, torch.bfloat16):
-            # torch's fused kernel (f32 statistics, one rounding of the product); it needs the
-            # gain in the activation dtype
-            return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
-        dtype = x.dtype
-        h = x.float()
-        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.eps)
-        return (h * self.weight.float()).to(dtype)
+        if x.is_cuda:
+            return rms_norm(x, self.weight, self.eps)
+        normalized = x.float() * torch.rsqrt(x.float().square().mean(-1, keepdim=True) + self.eps)
+        return normalized.to(x.dtype) * self.weight
 
 
 class SyntheticBlock(nn.Module):
