@@ -189,6 +189,9 @@ __device__ __forceinline__ float sum_squares(const float (&f)[8], float ss) {
   return ss;
 }
 
+// Rows of at most C * L chunks (every chunk of a row is held by its group). Each warp loads
+// the next rows it owns while it reduces and writes the current ones, so its loads stay in
+// flight across iterations.
 template <int KX, int KW, int L, int C>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(NormArgs a) {
   constexpr int G = 32 / L;  // rows per warp
@@ -197,29 +200,38 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(NormArgs a) {
   const int lane = threadIdx.x & (L - 1);
   const int g = (threadIdx.x & 31) / L;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kNormThreads + threadIdx.x) / 32;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * kNormThreads / 32;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kNormThreads / 32 * G;
   const int chunks = static_cast<int>(a.dim / 8);
   const float inv_dim = 1.0f / static_cast<float>(a.dim);
-  for (int64_t first = warp * G; first < a.rows; first += warps * G) {
+  Chunk<KX> next[C];
+  int64_t first = warp * G;
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    const int c = lane + i * L;
+    if (first + g < a.rows && c < chunks) next[i] = ldc<KX>(a.x, (first + g) * a.dim + c * 8);
+  }
+  for (; first < a.rows; first += stride) {
     const int64_t row = first + g;
     const bool live = row < a.rows;
     const int64_t base = row * a.dim;
     Chunk<KX> held[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) held[i] = next[i];
+    const int64_t ahead = row + stride;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = lane + i * L;
+      if (ahead < a.rows && c < chunks) next[i] = ldc<KX>(a.x, ahead * a.dim + c * 8);
+    }
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < C; ++i) {
       const int c = lane + i * L;
       if (live && c < chunks) {
-        held[i] = ldc<KX>(a.x, base + c * 8);
         float f[8];
         unpack<KX>(held[i], f);
         ss = sum_squares<KX>(f, ss);
       }
-    }
-    for (int c = lane + C * L; live && c < chunks; c += L) {
-      float f[8];
-      unpack<KX>(ldc<KX>(a.x, base + c * 8), f);
-      ss = sum_squares<KX>(f, ss);
     }
     ss = group_sum<L>(ss);
     if (!live) continue;
@@ -234,52 +246,67 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(NormArgs a) {
         norm_emit<KX, KW>(w, out, base, c, r, f);
       }
     }
-    for (int c = lane + C * L; c < chunks; c += L) {
-      float f[8];
-      unpack<KX>(ldc<KX>(a.x, base + c * 8), f);
-      norm_emit<KX, KW>(w, out, base, c, r, f);
-    }
   }
 }
 
-// Holds x between the passes and reads dy twice (the second read hits L1/L2).
+// Holds x and dy between the passes; the next rows' x and dy are loaded while the current
+// ones are reduced and written.
 template <int KX, int KW, int L, int C>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
+  constexpr int KY = promote(KX, KW);
   constexpr int G = 32 / L;
-  const void* const w = a.w;
-  const void* const dy = a.dy;
+  const void* const wp = a.w;
   void* const out = a.out;
   const int lane = threadIdx.x & (L - 1);
   const int g = (threadIdx.x & 31) / L;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kNormThreads + threadIdx.x) / 32;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * kNormThreads / 32;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kNormThreads / 32 * G;
   const int chunks = static_cast<int>(a.dim / 8);
   const float inv_dim = 1.0f / static_cast<float>(a.dim);
-  for (int64_t first = warp * G; first < a.rows; first += warps * G) {
+  Chunk<KX> nx[C];
+  Chunk<KY> ndy[C];
+  int64_t first = warp * G;
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    const int c = lane + i * L;
+    if (first + g < a.rows && c < chunks) {
+      nx[i] = ldc<KX>(a.x, (first + g) * a.dim + c * 8);
+      ndy[i] = ldc<KY>(a.dy, (first + g) * a.dim + c * 8);
+    }
+  }
+  for (; first < a.rows; first += stride) {
     const int64_t row = first + g;
     const bool live = row < a.rows;
     const int64_t base = row * a.dim;
     const float r = live ? __ldg(a.rstd_in + row) : 0.f;
     Chunk<KX> hx[C];
+    Chunk<KY> hdy[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      hx[i] = nx[i];
+      hdy[i] = ndy[i];
+    }
+    const int64_t ahead = row + stride;
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = lane + i * L;
+      if (ahead < a.rows && c < chunks) {
+        nx[i] = ldc<KX>(a.x, ahead * a.dim + c * 8);
+        ndy[i] = ldc<KY>(a.dy, ahead * a.dim + c * 8);
+      }
+    }
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < C; ++i) {
       const int c = lane + i * L;
       if (live && c < chunks) {
-        hx[i] = ldc<KX>(a.x, base + c * 8);
-        float x[8], dn[8];
+        float x[8], d[8], wv[8];
         unpack<KX>(hx[i], x);
-        norm_dn<KX, KW>(dy, w, base, c, dn);
+        unpack<KY>(hdy[i], d);
+        unpack<KW>(ldc<KW>(wp, c * 8), wv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dot = __fadd_rn(dot, __fmul_rn(dn[j], x[j]));
+        for (int j = 0; j < 8; ++j) dot = __fadd_rn(dot, __fmul_rn(rnd<KX>(rnd<KY>(__fmul_rn(d[j], wv[j]))), x[j]));
       }
-    }
-    for (int c = lane + C * L; live && c < chunks; c += L) {
-      float x[8], dn[8];
-      unpack<KX>(ldc<KX>(a.x, base + c * 8), x);
-      norm_dn<KX, KW>(dy, w, base, c, dn);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dot = __fadd_rn(dot, __fmul_rn(dn[j], x[j]));
     }
     dot = group_sum<L>(dot);
     if (!live) continue;
@@ -288,15 +315,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
     for (int i = 0; i < C; ++i) {
       const int c = lane + i * L;
       if (c < chunks) {
-        float x[8];
+        float x[8], d[8], wv[8], dx[8];
         unpack<KX>(hx[i], x);
-        norm_emit_dx<KX, KW>(dy, w, out, base, c, r, coef, x);
+        unpack<KY>(hdy[i], d);
+        unpack<KW>(ldc<KW>(wp, c * 8), wv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float dn = rnd<KX>(rnd<KY>(__fmul_rn(d[j], wv[j])));
+          dx[j] = rnd<KX>(__fsub_rn(__fmul_rn(dn, r), __fmul_rn(x[j], coef)));
+        }
+        st8<KX>(out, base + c * 8, dx);
       }
-    }
-    for (int c = lane + C * L; c < chunks; c += L) {
-      float x[8];
-      unpack<KX>(ldc<KX>(a.x, base + c * 8), x);
-      norm_emit_dx<KX, KW>(dy, w, out, base, c, r, coef, x);
     }
   }
 }
