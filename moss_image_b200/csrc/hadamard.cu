@@ -12,6 +12,7 @@
 //   radix 2 (last, odd log2(group)):  (a + b) * 0.70710678f, (a - b) * 0.70710678f
 // Explicit round-to-nearest intrinsics keep the compiler from contracting or reassociating.
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "errors.cuh"
@@ -145,48 +146,49 @@ constexpr int kFastTile = 4096;  // elements per tile: 16 per thread
 // lane at any power-of-two stride >= 16, hits 32 distinct banks
 __device__ __forceinline__ int padded(int e) { return e + (e >> 4); }
 
-template <int kKind>
-__device__ __forceinline__ void round_all(float (&v)[16], int n) {
+// Round 2N values to the 16-bit storage type and back (exact for every representable value):
+// one packed conversion per pair, the halves widened with integer ops.
+template <int kKind, int N>
+__device__ __forceinline__ void round_all(float (&v)[16]) {
   if constexpr (kKind == kF32) return;
 #pragma unroll
-  for (int i = 0; i < 16; i += 2) {
-    if (i >= n) break;
-    uint32_t w;
+  for (int i = 0; i < N; i += 2) {
     if constexpr (kKind == kBF16) {
       __nv_bfloat162 h = __floats2bfloat162_rn(v[i], v[i + 1]);
-      w = *reinterpret_cast<uint32_t*>(&h);
+      uint32_t w;
+      memcpy(&w, &h, sizeof(w));
       v[i] = __uint_as_float(w << 16);
       v[i + 1] = __uint_as_float(w & 0xffff0000u);
     } else {
-      __half2 h = __floats2half2_rn(v[i], v[i + 1]);
-      const float2 f = __half22float2(h);
+      const float2 f = __half22float2(__floats2half2_rn(v[i], v[i + 1]));
       v[i] = f.x;
       v[i + 1] = f.y;
     }
   }
 }
 
-// Radix-4 stage on register index bits (2b, 2b + 1) of 16 registers: quads {j, j + s, j + 2s,
-// j + 3s} with s = 4^b. out = (total - 2 x) * 0.5 computed as fma(-2, x, total) * 0.5 (2x is
-// exact, so the single rounding is the reference's).
-template <int kStride>
+// Radix-4 stage on register index bits (2b, 2b + 1) of N registers: quads {j, j + s, j + 2s,
+// j + 3s} with s = 4^b. The staged transform's (total - 2 x) * 0.5 is computed as
+// total * 0.5 - x: halving is exact and commutes with the rounding, so every value whose
+// magnitude stays in the normal range is identical, with one operation per output less.
+template <int kStride, int N>
 __device__ __forceinline__ void radix4(float (&v)[16]) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < N; ++j) {
     if ((j / kStride) % 4 != 0) continue;
     const float a = v[j], b = v[j + kStride], c = v[j + 2 * kStride], d = v[j + 3 * kStride];
-    const float total = __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
-    v[j] = __fmul_rn(__fmaf_rn(-2.0f, d, total), 0.5f);
-    v[j + kStride] = __fmul_rn(__fmaf_rn(-2.0f, c, total), 0.5f);
-    v[j + 2 * kStride] = __fmul_rn(__fmaf_rn(-2.0f, b, total), 0.5f);
-    v[j + 3 * kStride] = __fmul_rn(__fmaf_rn(-2.0f, a, total), 0.5f);
+    const float half = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d), 0.5f);
+    v[j] = __fsub_rn(half, d);
+    v[j + kStride] = __fsub_rn(half, c);
+    v[j + 2 * kStride] = __fsub_rn(half, b);
+    v[j + 3 * kStride] = __fsub_rn(half, a);
   }
 }
-template <int kStride>
+template <int kStride, int N>
 __device__ __forceinline__ void radix2(float (&v)[16]) {
   const float h = 0.7071067811865476f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < N; ++j) {
     if ((j / kStride) % 2 != 0) continue;
     const float a = v[j], b = v[j + kStride];
     v[j] = __fmul_rn(__fadd_rn(a, b), h);
@@ -194,51 +196,76 @@ __device__ __forceinline__ void radix2(float (&v)[16]) {
   }
 }
 
-// All stages of one phase with nb (1..4) active bits in register bits [0, nb).
-template <int kKind>
-__device__ __forceinline__ void phase_stages(float (&v)[16], int nb) {
-  const int n = 1 << nb;
-  if (nb >= 2) {
-    radix4<1>(v);
-    round_all<kKind>(v, n);
+// All stages of one phase with NB (1..4) index bits in register bits [0, NB).
+template <int kKind, int NB>
+__device__ __forceinline__ void phase_stages(float (&v)[16]) {
+  constexpr int N = 1 << NB;
+  if constexpr (NB >= 2) {
+    radix4<1, N>(v);
+    round_all<kKind, N>(v);
   }
-  if (nb == 4) {
-    radix4<4>(v);
-    round_all<kKind>(v, n);
-  } else if (nb == 3) {
-    radix2<4>(v);
-    round_all<kKind>(v, n);
-  } else if (nb == 1) {
-    radix2<1>(v);
-    round_all<kKind>(v, n);
+  if constexpr (NB == 4) {
+    radix4<4, N>(v);
+    round_all<kKind, N>(v);
+  } else if constexpr (NB == 3) {
+    radix2<4, N>(v);
+    round_all<kKind, N>(v);
+  } else if constexpr (NB == 1) {
+    radix2<1, N>(v);
+    round_all<kKind, N>(v);
   }
+}
+
+// Phase P (>= 1) of a tile held in shared memory: lines fix every index bit outside
+// [4P, 4P + NB); lanes vary the low bits so a warp touches distinct banks.
+template <int kKind, int LOG2G, int P>
+__device__ __forceinline__ void smem_phase(float* tile, int nrows) {
+  constexpr int kLow = 4 * P;
+  constexpr int kNB = (LOG2G - kLow) < 4 ? (LOG2G - kLow) : 4;
+  constexpr int kHiBits = LOG2G - kLow - kNB;
+  constexpr int kN = 1 << kNB;
+  const int lines = (nrows << LOG2G) >> kNB;
+  for (int line = threadIdx.x; line < lines; line += kThreads) {
+    const int lo = line & ((1 << kLow) - 1);
+    const int rest = line >> kLow;  // (row, high bits)
+    const int hi = rest & ((1 << kHiBits) - 1);
+    const int row = rest >> kHiBits;
+    const int base = (row << LOG2G) + lo + (hi << (kLow + kNB));
+    float w[16];
+#pragma unroll
+    for (int i = 0; i < kN; ++i) w[i] = tile[padded(base + (i << kLow))];
+    phase_stages<kKind, kNB>(w);
+#pragma unroll
+    for (int i = 0; i < kN; ++i) tile[padded(base + (i << kLow))] = w[i];
+  }
+  __syncthreads();
 }
 
 // Five CTAs per SM (48 registers): occupancy hides the load latency better than a
 // register-held prefetch of the next tile, which measured slower.
-template <int kKind>
+template <int kKind, int LOG2G>
 __global__ void __launch_bounds__(kThreads, 5)
-    hadamard_fast_kernel(const uint16_t* x, uint16_t* y, int64_t rows, int64_t cols,
-                         int log2g) {
-  __shared__ float tile[kFastTile + kFastTile / 16];
-  const int group = 1 << log2g;
-  const int rows_per_tile = kFastTile >> log2g;
-  const int64_t groups_per_row = cols >> log2g;
-  const int64_t row_tiles = (rows + rows_per_tile - 1) / rows_per_tile;
+    hadamard_fast_kernel(const uint16_t* x, uint16_t* y, int64_t rows, int64_t cols) {
+  constexpr int kGroup = 1 << LOG2G;
+  constexpr int kPhases = (LOG2G + 3) / 4;
+  constexpr int kRowsPerTile = kFastTile >> LOG2G;
+  __shared__ float tile[kPhases > 1 ? kFastTile + kFastTile / 16 : 1];
+  const int64_t groups_per_row = cols >> LOG2G;
+  const int64_t row_tiles = (rows + kRowsPerTile - 1) / kRowsPerTile;
   const int64_t tiles = row_tiles * groups_per_row;
   const int t = threadIdx.x;
-  const int nphase = (log2g + 3) / 4;
   for (int64_t tix = blockIdx.x; tix < tiles; tix += gridDim.x) {
-    const int64_t row0 = (tix / groups_per_row) * rows_per_tile;
-    const int64_t col0 = (tix % groups_per_row) << log2g;
-    const int nrows = static_cast<int>(std::min<int64_t>(rows_per_tile, rows - row0));
+    const int64_t row0 = (tix / groups_per_row) * kRowsPerTile;
+    const int64_t col0 = (tix % groups_per_row) << LOG2G;
+    const int nrows = static_cast<int>(std::min<int64_t>(kRowsPerTile, rows - row0));
     // phase 0: 16 contiguous elements of one row straight from global memory
     float v[16];
-    const int e0 = t * 16;  // element index within the tile (row-major rows of `group`)
-    const int r0 = e0 >> log2g;
+    const int e0 = t * 16;  // element index within the tile (row-major rows of the group)
+    const int r0 = e0 >> LOG2G;
     const bool live = r0 < nrows;
+    uint16_t* dst_row = y + (row0 + r0) * cols + col0 + (e0 & (kGroup - 1));
     if (live) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r0) * cols + col0 + (e0 & (group - 1)));
+      const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r0) * cols + col0 + (e0 & (kGroup - 1)));
       const uint4 u0 = src[0], u1 = src[1];
       const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
@@ -247,43 +274,23 @@ __global__ void __launch_bounds__(kThreads, 5)
           v[2 * k] = __uint_as_float(w[k] << 16);
           v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
         } else {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+          __half2 h2;
+          memcpy(&h2, &w[k], sizeof(h2));
+          const float2 f = __half22float2(h2);
           v[2 * k] = f.x;
           v[2 * k + 1] = f.y;
         }
       }
-      phase_stages<kKind>(v, log2g < 4 ? log2g : 4);
+      phase_stages<kKind, (LOG2G < 4 ? LOG2G : 4)>(v);
     }
-    if (nphase > 1) {
+    if constexpr (kPhases > 1) {
       if (live) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) tile[padded(e0 + i)] = v[i];
       }
       __syncthreads();
-      for (int p = 1; p < nphase; ++p) {
-        const int lowbits = 4 * p;
-        const int nb = min(4, log2g - lowbits);
-        const int lines = (nrows << log2g) >> nb;
-        // a line fixes every index bit outside [lowbits, lowbits + nb); lanes vary the low bits
-        for (int line = t; line < lines; line += kThreads) {
-          const int lo = line & ((1 << lowbits) - 1);
-          const int rest = line >> lowbits;  // (row, high bits)
-          const int hi_bits = log2g - lowbits - nb;
-          const int hi = rest & ((1 << hi_bits) - 1);
-          const int row = rest >> hi_bits;
-          const int base = (row << log2g) + lo + (hi << (lowbits + nb));
-          const int n = 1 << nb;
-          float w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (i < n) w[i] = tile[padded(base + (i << lowbits))];
-          phase_stages<kKind>(w, nb);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (i < n) tile[padded(base + (i << lowbits))] = w[i];
-        }
-        __syncthreads();
-      }
+      smem_phase<kKind, LOG2G, 1>(tile, nrows);
+      if constexpr (kPhases > 2) smem_phase<kKind, LOG2G, 2>(tile, nrows);
       if (live) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = tile[padded(e0 + i)];
@@ -296,15 +303,32 @@ __global__ void __launch_bounds__(kThreads, 5)
         if constexpr (kKind == kBF16) {
           w[k] = (__float_as_uint(v[2 * k]) >> 16) | (__float_as_uint(v[2 * k + 1]) & 0xffff0000u);
         } else {
-          __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-          w[k] = *reinterpret_cast<uint32_t*>(&h2);
+          const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+          memcpy(&w[k], &h2, sizeof(uint32_t));
         }
       }
-      uint4* dst = reinterpret_cast<uint4*>(y + (row0 + r0) * cols + col0 + (e0 & (group - 1)));
+      uint4* dst = reinterpret_cast<uint4*>(dst_row);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
       dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
     }
-    __syncthreads();  // the next tile reuses the shared memory
+    if constexpr (kPhases > 1) __syncthreads();  // the next tile reuses the shared memory
+  }
+}
+
+template <int kKind>
+void launch_fast(const void* x, void* y, int64_t rows, int64_t cols, int log2g, unsigned grid, cudaStream_t s) {
+  const uint16_t* xi = static_cast<const uint16_t*>(x);
+  uint16_t* yi = static_cast<uint16_t*>(y);
+  switch (log2g) {
+    case 4: hadamard_fast_kernel<kKind, 4><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 5: hadamard_fast_kernel<kKind, 5><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 6: hadamard_fast_kernel<kKind, 6><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 7: hadamard_fast_kernel<kKind, 7><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 8: hadamard_fast_kernel<kKind, 8><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 9: hadamard_fast_kernel<kKind, 9><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 10: hadamard_fast_kernel<kKind, 10><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 11: hadamard_fast_kernel<kKind, 11><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    default: hadamard_fast_kernel<kKind, 12><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
   }
 }
 
@@ -350,11 +374,9 @@ extern "C" int moss_hadamard_rotate(const void* x, int dtype, int64_t rows, int6
     const int64_t tiles = (rows + rows_per_tile - 1) / rows_per_tile * (cols / group);
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, 8LL * sm_count())));
     if (dtype == kBF16)
-      hadamard_fast_kernel<kBF16><<<grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y),
-                                                            rows, cols, log2g);
+      launch_fast<kBF16>(x, y, rows, cols, log2g, grid, s);
     else
-      hadamard_fast_kernel<kF16><<<grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<uint16_t*>(y),
-                                                           rows, cols, log2g);
+      launch_fast<kF16>(x, y, rows, cols, log2g, grid, s);
     MOSS_CUDA_TRY(cudaGetLastError());
     return clear_ok();
   }
