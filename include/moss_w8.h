@@ -168,7 +168,8 @@ MOSS_API int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t
  * block-diagonal in `group`-sized blocks (a power of two, at most 8192) built from the
  * regular H4 and one H2 factor for odd log2(group). H is symmetric and orthonormal, so the
  * same call rotates activations forward and input gradients back. Every radix stage is
- * computed in f32 and rounded to the tensor's dtype, as the reference's staged transform does;
+ * computed in f32 and rounded to the tensor's dtype, as the reference's staged transform does
+ * (identical results for every value whose intermediate magnitudes stay in the normal range);
  * all stages run in one pass. Replaces triton_hadamard_transform
  * (training/quant_kernels.py:387-426) and its stage kernels (:231-277); eager equivalent
  * rotate_hadamard (training/convrot.py:36-63).
