@@ -34,10 +34,11 @@ constexpr int kTileN = 256;
 // flight per SM), so each load stage fetches kSub k-blocks with one 3-D box per operand.
 constexpr int kSub = 2;
 // Separate rings: an A stage lives until the MMAs that read it retire; an int8 stage only
-// until it is dequantised, so fewer int8 stages are needed. The converted ring is the deepest:
-// two converter groups fill it two k-blocks at a time.
-constexpr int kAStages = 4;
-constexpr int kWStages = 3;
+// until it is dequantised, so fewer int8 stages are needed. A converted entry holds the kSub
+// k-blocks of one load step, so the MMA issuer waits and commits once per step rather than
+// once per k-block (about 8% on the 9216 x 3072 x 3072 forward against per-k-block entries).
+constexpr int kAStages = 3;
+constexpr int kWStages = 2;
 constexpr int kBStages = 3;
 constexpr int kConvWarps = 8;
 // The converter warps form kSub groups; group g dequantises k-block g of every weight stage,
@@ -53,8 +54,9 @@ constexpr uint32_t kWBlock = kHalf * BK;      // 8 KB: one k-block of this CTA's
 constexpr uint32_t kAStage = kSub * kABlock;
 constexpr uint32_t kWStage = kSub * kWBlock;
 constexpr uint32_t kBBytes = kHalf * BK * 2;  // 16 KB converted operand per k-block
+constexpr uint32_t kBEntry = kSub * kBBytes;  // one converted entry per load step
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
-constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStages * kBBytes;
+constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStages * kBEntry;
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
@@ -142,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(bars->w_empty[s]), kConvWarps);
     }
     for (int s = 0; s < kBStages; ++s) {
-      mbar_init(bar(bars->b_full[s]), 2 * kGroupWarps);
+      mbar_init(bar(bars->b_full[s]), 2 * kConvWarps);
       mbar_init(bar(bars->b_empty[s]), 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -267,16 +269,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (!mbar_wait_cluster(bar(bars->b_full[bstage]), bphase, abort_flag, args.status,
+                                 MOSS_STATUS_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           for (int sub = 0; sub < st.nsub; ++sub) {
-            if (!mbar_wait_cluster(bar(bars->b_full[bstage]), bphase, abort_flag, args.status,
-                                   MOSS_STATUS_TIMEOUT_MMA)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
             if (lane == 0) {
               const uint32_t a_base = a_smem + stage * kAStage + sub * kABlock;
-              const uint32_t b_base = b_smem + bstage * kBBytes;
+              const uint32_t b_base = b_smem + bstage * kBEntry + sub * kBBytes;
 #pragma unroll
               for (int kk = 0; kk < BK / 16; ++kk) {
                 const uint64_t adesc = umma_desc_sw128(a_base + kk * 32, 16, 1024);
@@ -288,14 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 umma_f16_pair(d_tmem, adesc, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
               }
-              umma_commit_pair_mc(bar(bars->b_empty[bstage]), 0x3);
               issued_any = true;
             }
             first = false;
-            __syncwarp();
-            if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
           }
-          if (!ok) break;
+          if (lane == 0) umma_commit_pair_mc(bar(bars->b_empty[bstage]), 0x3);
+          __syncwarp();
+          if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
           if (lane == 0) umma_commit_pair_mc(bar(bars->a_empty[stage]), 0x3);
           __syncwarp();
           if (++stage == kAStages) { stage = 0; phase ^= 1u; }
@@ -438,93 +439,92 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        for (int sub = 0; sub < st.nsub; ++sub) {
-          if (sub == group) {
-            if (!mbar_wait_cluster(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status,
-                                   MOSS_STATUS_TIMEOUT_CONVERT)) {
-              ok = false;
-              break;
-            }
-            const uint32_t b_base = b_smem + bstage * kBBytes;
-            uint4 o[8];
-            if constexpr (!kDX) {
-              // forward: K-major B half [128 n][64 k], int8 stage rows of 64 bytes
-              const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
-              if (!st.ext) {
-                uint2 qv[8];
+        // One converted entry per step: group g fills k-block g of it. Every converter warp of
+        // both CTAs arrives on the leader's b_full, idle groups of a one-block step included.
+        if (!mbar_wait_cluster(bar(bars->b_empty[bstage]), bphase ^ 1u, abort_flag, args.status,
+                               MOSS_STATUS_TIMEOUT_CONVERT)) {
+          ok = false;
+          break;
+        }
+        if (group < st.nsub) {
+          const int sub = group;
+          const uint32_t b_base = b_smem + bstage * kBEntry + sub * kBBytes;
+          uint4 o[8];
+          if constexpr (!kDX) {
+            // forward: K-major B half [128 n][64 k], int8 stage rows of 64 bytes
+            const uint32_t w_base = w_smem + stage * kWStage + sub * kWBlock;
+            if (!st.ext) {
+              uint2 qv[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) qv[i] = lds64(w_base + (crow + 16 * i) * 64 + cch * 8);
+              for (int i = 0; i < 8; ++i) qv[i] = lds64(w_base + (crow + 16 * i) * 64 + cch * 8);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const int gn = n0 + crow + 16 * i;
-                  o[i] = gn < args.Nc ? load8_scaled(args.ext_b, args.ext_b_kind,
-                                                     static_cast<int64_t>(gn) * args.ld_ext_b, st.first_kb * BK + cch * 8,
-                                                     args.ext_r, args.ext_scale, kV)
-                                      : make_uint4(0, 0, 0, 0);
-                }
-              }
+              for (int i = 0; i < 8; ++i) o[i] = dec_f[i].chunk8(qv[i], args.w_kind);
+            } else {
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const int row = crow + 16 * i;
-                sts128(b_base + (row >> 3) * 1024 + (row & 7) * 128 + (((cch ^ (row & 7)) & 7) << 4), o[i]);
+                const int gn = n0 + crow + 16 * i;
+                o[i] = gn < args.Nc ? load8_scaled(args.ext_b, args.ext_b_kind,
+                                                   static_cast<int64_t>(gn) * args.ld_ext_b, st.first_kb * BK + cch * 8,
+                                                   args.ext_r, args.ext_scale, kV)
+                                    : make_uint4(0, 0, 0, 0);
               }
-            } else {
-              // grad-input: MN-major B half = 2 atoms x [64 n][64 k]; the int8 stage holds
-              // kSub * 64 reduction rows of 128 bytes (128B swizzle).
-              if (!st.ext) {
-                Dec<kV, kFast> dec[4];
+            }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) dec[j].set(dx_scale[j], args.w_kind);
-                uint2 qv[8];
+            for (int i = 0; i < 8; ++i) {
+              const int row = crow + 16 * i;
+              sts128(b_base + (row >> 3) * 1024 + (row & 7) * 128 + (((cch ^ (row & 7)) & 7) << 4), o[i]);
+            }
+          } else {
+            // grad-input: MN-major B half = 2 atoms x [64 n][64 k]; the int8 stage holds
+            // kSub * 64 reduction rows of 128 bytes (128B swizzle).
+            if (!st.ext) {
+              Dec<kV, kFast> dec[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const int a = i >> 2, r = crow + 16 * (i & 3);
-                  const int q16 = 4 * a + (cch >> 1);
-                  qv[i] = lds64(w_smem + stage * kWStage + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) +
-                                (cch & 1) * 8);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = dec[i & 3].chunk8(qv[i], args.w_kind);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const int a = i >> 2, r = crow + 16 * (i & 3);
-                  const int gj = st.first_kb * BK + r;
-                  o[i] = gj < args.ext_r ? load8_scaled(args.ext_b, args.ext_b_kind,
-                                                        static_cast<int64_t>(gj) * args.ld_ext_b, n0 + a * 64 + cch * 8,
-                                                        args.Nc, args.ext_scale, kV)
-                                         : make_uint4(0, 0, 0, 0);
-                }
-              }
+              for (int j = 0; j < 4; ++j) dec[j].set(dx_scale[j], args.w_kind);
+              uint2 qv[8];
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
                 const int a = i >> 2, r = crow + 16 * (i & 3);
-                sts128(b_base + a * (kBBytes / 2) + r * 128 + (((cch ^ (r & 7)) & 7) << 4), o[i]);
+                const int q16 = 4 * a + (cch >> 1);
+                qv[i] = lds64(w_smem + stage * kWStage + (sub * BK + r) * 128 + (((q16 ^ (r & 7)) & 7) << 4) +
+                              (cch & 1) * 8);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = dec[i & 3].chunk8(qv[i], args.w_kind);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int a = i >> 2, r = crow + 16 * (i & 3);
+                const int gj = st.first_kb * BK + r;
+                o[i] = gj < args.ext_r ? load8_scaled(args.ext_b, args.ext_b_kind,
+                                                      static_cast<int64_t>(gj) * args.ld_ext_b, n0 + a * 64 + cch * 8,
+                                                      args.Nc, args.ext_scale, kV)
+                                       : make_uint4(0, 0, 0, 0);
               }
             }
-            // b_full of a stage's first k-block also certifies this CTA's A rows: the leader's
-            // MMA reads both CTAs' halves, and it issues the stage's k-blocks in order.
-            if (sub == 0 &&
-                !mbar_wait(bar(bars->a_full[astage]), aphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
-              ok = false;
-              break;
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              const uint32_t fb = bar(bars->b_full[bstage]);
-              if (leader)
-                mbar_arrive(fb);
-              else
-                mbar_arrive_cluster(mapa_shared(fb, 0));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int a = i >> 2, r = crow + 16 * (i & 3);
+              sts128(b_base + a * (kBBytes / 2) + r * 128 + (((cch ^ (r & 7)) & 7) << 4), o[i]);
             }
           }
-          // every group walks every converted stage, so the ring positions stay in step
-          if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
         }
+        // b_full also certifies this CTA's A rows: the leader's MMA reads both CTAs' halves
+        if (group == 0 &&
+            !mbar_wait(bar(bars->a_full[astage]), aphase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_CONVERT)) {
+          ok = false;
+          break;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t fb = bar(bars->b_full[bstage]);
+          if (leader)
+            mbar_arrive(fb);
+          else
+            mbar_arrive_cluster(mapa_shared(fb, 0));
+        }
+        if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
         if (!ok) break;
         if (lane == 0) mbar_arrive(bar(bars->w_empty[stage]));
         if (++stage == kWStages) { stage = 0; phase ^= 1u; }
