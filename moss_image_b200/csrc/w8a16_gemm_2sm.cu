@@ -58,6 +58,7 @@ constexpr uint32_t kBEntry = kSub * kBBytes;  // one converted entry per load st
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
 constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStages * kBEntry;
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
+static_assert(kSmemBytes <= 227 * 1024, "rings exceed the 227 KB of shared memory a CTA may use");
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
 // LoRA k-block. Every role walks the same sequence. Tiles in flight at the same time walk K
