@@ -82,10 +82,15 @@ MOSS_API int moss_w8_dequantize(const int8_t* q, const float* scale, int64_t n, 
 
 /*
  * Scratch bytes the GEMM entry points use for the given problem (k_red = reduction length,
- * n_out = output columns), 0 when none. Small-M problems split the reduction across CTAs
- * (split-K) and exchange f32 partial tiles through this workspace; with a NULL or smaller
- * workspace they run unsplit (same result, lower occupancy). New in this library: the
- * reference's Triton launchers take no workspace (training/quant_kernels.py:294-373).
+ * n_out = output columns), 0 when none. Two cases split the reduction across CTAs and
+ * exchange f32 partial tiles through this workspace: small-M problems (split-K over every
+ * tile), and CTA-pair problems whose 256 x 256 tiles leave the last round of the persistent
+ * grid partly empty (only that round's tiles are split, so idle SM pairs share them; at most
+ * about 19 MB). With a NULL or smaller workspace they run unsplit: lower occupancy, and a
+ * result that can differ in the last bit of some outputs, since the f32 partial sums are
+ * grouped differently. Either way the result is deterministic for a given call. New in this
+ * library: the reference's Triton launchers take no workspace
+ * (training/quant_kernels.py:294-373).
  */
 MOSS_API int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t k_red, size_t* bytes);
 
@@ -126,8 +131,9 @@ MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t 
  *   - The first call on a device, with that device current, looks up the array's device
  *     address (cudaGetSymbolAddress) and caches it; make that first call before any stream
  *     capture.
- *   - Problems whose moss_w8a16_gemm_workspace_bytes(m, n, k) exceeds the array are refused
- *     with MOSS_ERR_INVALID_ARGUMENT before any launch; use moss_w8a16_gemm_fwd for them.
+ *   - Small-M problems whose moss_w8a16_gemm_workspace_bytes(m, n, k) exceeds the array are
+ *     refused with MOSS_ERR_INVALID_ARGUMENT before any launch; use moss_w8a16_gemm_fwd for
+ *     them. CTA-pair problems whose last-round split would not fit run without that split.
  *   - All calls on a device share the one array and it keeps the previous call's contents:
  *     each call clears the split-K counters on its stream, and the partial tiles are written
  *     before they are read. Calls whose kernels can overlap on the GPU (different streams

@@ -30,6 +30,10 @@ struct Args {
   int splits, kb_per_split;
   float* partial;
   int* counters;
+  // CTA-pair kernel, last partial wave: tiles [tail_first, tiles) are split along K into
+  // tail_splits units each, whose f32 partials go to `partial` [tail tile][split][256][256]
+  // and are summed by a reduction kernel after the GEMM. tail_first = tiles: no split.
+  int tail_first, tail_splits;
 };
 
 // k-block schedule of one work unit: iteration i -> weight k-block or LoRA block.
@@ -114,6 +118,18 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 // CTA-pair (cta_group::2) launcher, defined in w8a16_gemm_2sm.cu. Builds its own tensor maps;
 // returns MOSS_ERR_UNSUPPORTED (without launching) when the shapes do not fit it.
 int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t stream);
+
+// Split of the CTA-pair kernel's last partial wave (defined in w8a16_gemm_2sm.cu). When the
+// 256 x 256 tiles leave the final round of the persistent grid partly empty, that round's
+// tiles are cut along K so every pair gets a share; the planner depends only on the shape
+// (not on a LoRA term), so the workspace query and the launch agree.
+struct PairTailPlan {
+  int tail_first = 0;  // first split tile (= number of tiles when nothing is split)
+  int splits = 1;
+  size_t partial_bytes = 0;
+  size_t total() const { return splits > 1 ? partial_bytes : 0; }
+};
+PairTailPlan plan_pair_tail(int64_t M, int64_t Nc, int64_t Kr, int sms);
 
 // Operand-swapped kernel (w8a16_gemm_skinny.cu): any M without a LoRA term, used when the
 // CTA-pair kernel would leave SMs idle.

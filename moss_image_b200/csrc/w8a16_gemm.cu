@@ -659,6 +659,8 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.kb_per_split = a.main_kb;
   a.partial = nullptr;
   a.counters = nullptr;
+  a.tail_first = a.tiles_m * a.tiles_n;  // the CTA-pair kernel's last-round split: none
+  a.tail_splits = 1;
 
   CUtensorMap ta, tw, te;
   memset(&ta, 0, sizeof(ta));
@@ -704,6 +706,15 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
     Args a2 = a;
     a2.tiles_m = static_cast<int>((M + 255) / 256);
     a2.tiles_n = static_cast<int>((Nc + 255) / 256);
+    a2.tail_first = a2.tiles_m * a2.tiles_n;
+    a2.tail_splits = 1;
+    const PairTailPlan tp = plan_pair_tail(M, Nc, Kr, sms);
+    if (tp.splits > 1 && workspace != nullptr && workspace_bytes >= tp.total() &&
+        (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+      a2.tail_first = tp.tail_first;
+      a2.tail_splits = tp.splits;
+      a2.partial = static_cast<float*>(workspace);
+    }
     const int rc = launch_pair(dx, v_kind, fast, a2, stream);
     if (rc != MOSS_ERR_UNSUPPORTED) return rc;
   }
@@ -729,7 +740,11 @@ extern "C" int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t
   *bytes = 0;
   if (m <= 0 || n_out <= 0 || k_red <= 0) return clear_ok();
   const int sms = gemm::sm_count();
-  if (gemm::use_pair(m, n_out, sms)) return clear_ok();
+  if (gemm::use_pair(m, n_out, sms)) {
+    // the CTA-pair kernel's split of its last, partly empty round of tiles
+    *bytes = gemm::plan_pair_tail(m, n_out, k_red, sms).total();
+    return clear_ok();
+  }
   // Enough for whichever kernel the call picks: the few-row kernel (no LoRA term) or the
   // 1-CTA kernel's split-K (with one).
   size_t need = gemm::plan_split(m, n_out, k_red, sms).total();
@@ -817,6 +832,8 @@ extern "C" int moss_w8a16_gemm_fwd_noalloc(const void* x, int x_dtype, int64_t m
   size_t need = 0;
   rc = moss_w8a16_gemm_workspace_bytes(m, n, k, &need);
   if (rc != MOSS_OK) return rc;
+  if (need > gemm::kNoAllocScratchBytes && gemm::use_pair(m, n, gemm::sm_count()))
+    need = 0;  // the CTA-pair kernel then runs without splitting its last round of tiles
   if (need > gemm::kNoAllocScratchBytes)
     return fail(MOSS_ERR_INVALID_ARGUMENT,
                 "moss_w8a16_gemm_fwd_noalloc: m=%lld n=%lld k=%lld needs %zu bytes of split-K scratch, more than "
@@ -826,7 +843,7 @@ extern "C" int moss_w8a16_gemm_fwd_noalloc(const void* x, int x_dtype, int64_t m
   // The split-K counters are cleared on the stream inside run() before the kernel; the f32
   // partials are always written before they are read, so stale contents are harmless.
   rc = gemm::run(false, x, x_dtype, m, k, n, q, scale, weight_dtype, n, k, bias, bias_dtype, lora_xa, lora_b,
-                 lora_b_dtype, lora_rank, lora_scale, y, y_dtype, scratch, need, status,
+                 lora_b_dtype, lora_rank, lora_scale, y, y_dtype, need > 0 ? scratch : nullptr, need, status,
                  reinterpret_cast<cudaStream_t>(stream));
   return rc == MOSS_OK ? clear_ok() : rc;
 }

@@ -15,6 +15,7 @@
 // bytes per FLOP (each SM loads half of the int8 tile).
 // The decode rounding is identical (dequant.cuh).
 #include <algorithm>
+#include <cstdint>
 #include <mutex>
 
 #include "common.cuh"
@@ -58,6 +59,10 @@ constexpr uint32_t kBEntry = kSub * kBBytes;  // one converted entry per load st
 constexpr uint32_t kTmemCols = 512;           // two 256-column accumulators
 constexpr uint32_t kDataBytes = kAStages * kAStage + kWStages * kWStage + kBStages * kBEntry;
 constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
+// Last-round split (plan_pair_tail): at most this many units per tile, and only when it saves
+// at least this many load steps of the tail round.
+constexpr int64_t kMaxTailSplits = 16;
+constexpr int64_t kMinTailGainSteps = 8;
 static_assert(kSmemBytes <= 227 * 1024, "rings exceed the 227 KB of shared memory a CTA may use");
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
@@ -86,6 +91,36 @@ __device__ __forceinline__ int steps_per_tile(const Args& a) {
   return (a.main_kb + kSub - 1) / kSub + (a.num_kb - a.main_kb);
 }
 
+// Work unit of the persistent loop: whole tiles first, then the tiles of the last partial
+// round, each cut into `tail_splits` ranges of load steps. Every role walks the same units.
+struct Unit {
+  int tile;
+  int s0, s1;  // load steps [s0, s1)
+  int tail;    // index among the split tiles; -1 for a whole tile
+  int split;
+};
+__device__ __forceinline__ int units_of(const Args& a) {
+  return a.tail_first + (a.tiles_m * a.tiles_n - a.tail_first) * a.tail_splits;
+}
+__device__ __forceinline__ Unit unit_of(const Args& a, int u, int nsteps) {
+  Unit w;
+  if (u < a.tail_first) {
+    w.tile = u;
+    w.s0 = 0;
+    w.s1 = nsteps;
+    w.tail = -1;
+    w.split = 0;
+  } else {
+    const int v = u - a.tail_first;
+    w.tail = v / a.tail_splits;
+    w.split = v - w.tail * a.tail_splits;
+    w.tile = a.tail_first + w.tail;
+    w.s0 = w.split * nsteps / a.tail_splits;
+    w.s1 = (w.split + 1) * nsteps / a.tail_splits;
+  }
+  return w;
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                                             int c2) {
   asm volatile(
@@ -93,6 +128,88 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// f32 partial of a split tile: [tail tile][split][256 tile rows][256 tile columns].
+__device__ __forceinline__ float* partial_at(const Args& a, int tail, int split, int lrow, int lcol) {
+  return a.partial + ((static_cast<int64_t>(tail) * a.tail_splits + split) * kTileM + lrow) * kTileN + lcol;
+}
+
+// Bias (forward) and the rounded store of 32 consecutive outputs of one row.
+template <bool kDX, int kV>
+__device__ __forceinline__ void store_out32(const Args& args, float (&v)[32], int row, int col0, bool vec_ok) {
+  if constexpr (!kDX) {
+    if (args.bias != nullptr) {
+      float b[32];
+      load_bias32<kV>(args.bias, args.bias_kind, col0, args.Nc, b);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += b[j];
+    }
+  }
+  const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
+  if (args.out_kind == kV && vec_ok && col0 + 32 <= args.Nc) {
+    // 64 contiguous bytes per thread as two full 32-byte sectors
+    uint32_t p0[8], p1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      p0[j] = pack2_kind<kV>(v[2 * j], v[2 * j + 1]);
+      p1[j] = pack2_kind<kV>(v[16 + 2 * j], v[16 + 2 * j + 1]);
+    }
+    uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
+    stg256(dst, p0);
+    stg256(dst + 16, p1);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
+  }
+}
+
+// Finishes the split tiles of the last round: the units' f32 partials summed in split order
+// (so the result does not depend on which unit ran first), plus the bias, rounded to the
+// output kind. One thread per 4 consecutive columns of a tile row; a warp covers 512
+// contiguous bytes of one partial row, so every load is coalesced.
+template <bool kDX, int kV>
+__global__ void __launch_bounds__(256) pair_tail_reduce_kernel(const Args args) {
+  constexpr int kQuads = kTileN / 4;
+  const int64_t total = static_cast<int64_t>(args.tiles_m * args.tiles_n - args.tail_first) * kTileM * kQuads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int quad = static_cast<int>(i % kQuads);
+    const int lrow = static_cast<int>((i / kQuads) % kTileM);
+    const int tail = static_cast<int>(i / (static_cast<int64_t>(kQuads) * kTileM));
+    int m_blk, n_blk;
+    tile_coords(args.tail_first + tail, args.tiles_m, args.tiles_n, m_blk, n_blk);
+    const int row = m_blk * kTileM + lrow;
+    const int col = n_blk * kTileN + quad * 4;
+    if (row >= args.M || col >= args.Nc) continue;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(partial_at(args, tail, 0, lrow, quad * 4)));
+    for (int sp = 1; sp < args.tail_splits; ++sp) {
+      const float4 f = __ldcg(reinterpret_cast<const float4*>(partial_at(args, tail, sp, lrow, quad * 4)));
+      acc.x += f.x;
+      acc.y += f.y;
+      acc.z += f.z;
+      acc.w += f.w;
+    }
+    float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if constexpr (!kDX) {
+      if (args.bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (col + j < args.Nc) v[j] += round_to_kind(load_as_float(args.bias, args.bias_kind, col + j), kV);
+      }
+    }
+    const int64_t off = static_cast<int64_t>(row) * args.ldo + col;
+    if (args.out_kind == kV && col + 4 <= args.Nc && (off & 3) == 0 &&
+        (reinterpret_cast<uintptr_t>(args.out) & 7) == 0) {
+      const uint2 p = make_uint2(pack2_kind<kV>(v[0], v[1]), pack2_kind<kV>(v[2], v[3]));
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(args.out) + off) = p;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (col + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
+    }
+  }
 }
 
 struct Barriers {
@@ -132,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool leader = rank == 0;
   const int pair_id = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_units = units_of(args);
   const int nsteps = steps_per_tile(args);
 
   if (threadIdx.x == 0) {
@@ -184,12 +301,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t used_mask = 0, last_phase_mask = 0;
     bool ok = true;
-    for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+    for (int u = pair_id; u < num_units && ok; u += num_pairs) {
+      const Unit w = unit_of(args, u, nsteps);
       int m_blk, n_blk;
-      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
-      for (int si = 0; si < nsteps; ++si) {
+      for (int si = w.s0; si < w.s1; ++si) {
         const Step st = step_of(si, args.main_kb);
         const uint32_t empty_bar = a_role ? bar(bars->a_empty[stage]) : bar(bars->w_empty[stage]);
         if (!mbar_wait_cluster(empty_bar, phase ^ 1u, abort_flag, args.status, MOSS_STATUS_TIMEOUT_LOAD)) {
@@ -253,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int t = pair_id; t < num_tiles && ok; t += num_pairs, ++it) {
+      for (int u = pair_id; u < num_units && ok; u += num_pairs, ++it) {
+        const Unit w = unit_of(args, u, nsteps);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait_cluster(bar(bars->acc_empty[acc]), acc_phase ^ 1u, abort_flag, args.status,
@@ -264,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
         bool first = true;
-          for (int si = 0; si < nsteps && ok; ++si) {
+        for (int si = w.s0; si < w.s1 && ok; ++si) {
           const Step st = step_of(si, args.main_kb);
           if (!mbar_wait_cluster(bar(bars->a_full[stage]), phase, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA)) {
             ok = false;
@@ -322,7 +441,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;
     int it = 0;
-    for (int t = pair_id; t < num_tiles; t += num_pairs, ++it) {
+    for (int u = pair_id; u < num_units; u += num_pairs, ++it) {
+      const Unit w = unit_of(args, u, nsteps);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_cluster(bar(bars->acc_full[acc]), acc_phase, abort_flag, args.status,
@@ -330,10 +450,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       tc_fence_after();
       int m_blk, n_blk;
-      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
-      const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      const int lrow = static_cast<int>(rank) * kHalf + q * 32 + lane;  // row within the tile
+      const int row = m_blk * kTileM + lrow;
       const int n0 = n_blk * kTileN;
-      const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
       const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 15) == 0) &&
                           ((reinterpret_cast<uintptr_t>(args.out) & 31) == 0);
@@ -357,34 +477,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int col0 = n0 + c * 32;
         if (col0 >= args.Nc || !row_ok) continue;
+        if (w.tail >= 0) {
+          // split tile: this unit's f32 partial, summed by pair_tail_reduce_kernel
+          float* dst = partial_at(args, w.tail, w.split, lrow, c * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t p[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[e] = r[8 * j + e];
+            stg256(dst + 8 * j, p);
+          }
+          continue;
+        }
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if constexpr (!kDX) {
-          if (args.bias != nullptr) {
-            float b[32];
-            load_bias32<kV>(args.bias, args.bias_kind, col0, args.Nc, b);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += b[j];
-          }
-        }
-        const int64_t off = static_cast<int64_t>(row) * args.ldo + col0;
-        if (args.out_kind == kV && vec_ok && col0 + 32 <= args.Nc) {
-          // 64 contiguous bytes per thread as two full 32-byte sectors
-          uint32_t p0[8], p1[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            p0[j] = pack2_kind<kV>(v[2 * j], v[2 * j + 1]);
-            p1[j] = pack2_kind<kV>(v[16 + 2 * j], v[16 + 2 * j + 1]);
-          }
-          uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
-          stg256(dst, p0);
-          stg256(dst + 16, p1);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < args.Nc) store_from_float(args.out, args.out_kind, off + j, round_to_kind(v[j], kV));
-        }
+        store_out32<kDX, kV>(args, v, row, col0, vec_ok);
       }
     }
   } else if (warp >= kConvWarp0) {
@@ -401,30 +509,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     // forward: the row scales of the next tile are requested while this one is converted
     float next_scale[8];
-    auto load_tile_scales = [&](int t_next) {
+    auto load_unit_scales = [&](int u_next) {
       if constexpr (!kDX) {
-        int mb, nb;
-        tile_coords(t_next, args.tiles_m, args.tiles_n, mb, nb);
+        const bool valid = u_next < num_units;
+        int mb = 0, nb = 0;
+        if (valid) tile_coords(unit_of(args, u_next, nsteps).tile, args.tiles_m, args.tiles_n, mb, nb);
         const int base_n = nb * kTileN + static_cast<int>(rank) * kHalf;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int gn = base_n + crow + 16 * i;
-          next_scale[i] = (t_next < num_tiles && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
+          next_scale[i] = (valid && gn < args.w_rows) ? __ldg(args.scale + gn) : 0.0f;
         }
       }
     };
-    load_tile_scales(pair_id);
-    for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+    load_unit_scales(pair_id);
+    for (int u = pair_id; u < num_units && ok; u += num_pairs) {
+      const Unit w = unit_of(args, u, nsteps);
       int m_blk, n_blk;
-      tile_coords(t, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
       Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) dec_f[i].set(next_scale[i], args.w_kind);
-        load_tile_scales(t + num_pairs);
+        load_unit_scales(u + num_pairs);
       }
-      for (int si = 0; si < nsteps && ok; ++si) {
+      for (int si = w.s0; si < w.s1 && ok; ++si) {
         const Step st = step_of(si, args.main_kb);
         // grad-input: the row scales of this group's k-block depend only on the k-block index,
         // so they are requested before the waits instead of inside the conversion chain
@@ -591,8 +701,8 @@ static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUte
     max_pairs = clusters;
   });
   MOSS_CUDA_TRY(attr_err);
-  const int tiles = a.tiles_m * a.tiles_n;
-  const int pairs = std::max(1, std::min(tiles, max_pairs));
+  const int units = a.tail_first + (a.tiles_m * a.tiles_n - a.tail_first) * a.tail_splits;
+  const int pairs = std::max(1, std::min(units, max_pairs));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -606,10 +716,38 @@ static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUte
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   MOSS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tw, te, a));
+  if (a.tail_splits > 1) {
+    const int64_t quads = static_cast<int64_t>(a.tiles_m * a.tiles_n - a.tail_first) * kTileM * (kTileN / 4);
+    const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, 8LL * sm_count()));
+    pair_tail_reduce_kernel<kDX, kV><<<blocks, 256, 0, stream>>>(a);
+    MOSS_CUDA_TRY(cudaGetLastError());
+  }
   return MOSS_OK;
 }
 
 }  // namespace pair
+
+PairTailPlan plan_pair_tail(int64_t M, int64_t Nc, int64_t Kr, int sms) {
+  using namespace pair;
+  PairTailPlan p;
+  const int64_t tiles = ((M + kTileM - 1) / kTileM) * ((Nc + kTileN - 1) / kTileN);
+  p.tail_first = static_cast<int>(std::min<int64_t>(tiles, INT32_MAX));
+  const int64_t pairs = sms / 2;
+  const int64_t steps = ((Kr + BK - 1) / BK + kSub - 1) / kSub;
+  if (tiles <= 0 || pairs <= 0 || tiles > INT32_MAX) return p;
+  const int64_t tail = tiles % pairs;
+  if (tail == 0) return p;
+  // As many splits as the idle pairs of the last round allow, each at least one load step.
+  const int64_t splits = std::min<int64_t>(pairs / tail, std::min<int64_t>(steps, kMaxTailSplits));
+  if (splits < 2) return p;
+  // The split must save more load steps (about 1 us each on a 256 x 256 tile) than the
+  // partials' round trip through L2 and the reduction launch cost.
+  if (steps - (steps + splits - 1) / splits < kMinTailGainSteps) return p;
+  p.tail_first = static_cast<int>(tiles - tail);
+  p.splits = static_cast<int>(splits);
+  p.partial_bytes = static_cast<size_t>(tail * splits) * kTileM * kTileN * sizeof(float);
+  return p;
+}
 
 int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t s) {
   using namespace pair;

@@ -68,3 +68,49 @@ def test_empty_problems_are_no_ops_without_device_work():
     size = ctypes.c_size_t(123)
     assert lib.moss_w8a16_gemm_workspace_bytes(0, 8, 16, ctypes.byref(size)) == _lib.MOSS_OK and size.value == 0
     assert lib.moss_w8_quantize(None, 1, 0, 16, None, None, None, None) == _lib.MOSS_OK
+
+
+def _sm_count() -> int:
+    """SMs the library plans for: the device's count, or 148 (B200) when no GPU is visible."""
+    import torch
+
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(0).multi_processor_count
+    return 148
+
+
+def _expected_pair_tail_bytes(m: int, n_out: int, k_red: int, sms: int) -> int:
+    """The CTA-pair kernel's last-round split, restated: tiles of 256 x 256, one tile per SM
+    pair per round; the tiles of a partly empty last round are cut along K into as many
+    units as the idle pairs allow (at most 16, each at least one load step of two 64-wide
+    k-blocks), when that saves at least 8 load steps. Scratch: one f32 256 x 256 partial
+    per unit."""
+    tiles = -(-m // 256) * -(-n_out // 256)
+    pairs = sms // 2
+    steps = -(-(-(-k_red // 64)) // 2)
+    tail = tiles % pairs
+    if tail == 0:
+        return 0
+    splits = min(pairs // tail, steps, 16)
+    if splits < 2 or steps - -(-steps // splits) < 8:
+        return 0
+    return tail * splits * 256 * 256 * 4
+
+
+@pytest.mark.parametrize("m,n_out,k_red", [
+    (2048, 3072, 3072),    # 96 tiles: 22 in the last round of 74 pairs, split 3 ways
+    (8192, 3072, 3072),    # 384 tiles: 14 left over, split 5 ways
+    (8192, 18432, 3072),   # 2304 tiles: 10 left over, split 7 ways
+    (9216, 3072, 3072),    # 432 tiles: 62 left over, no room to split
+    (9216, 12288, 3072),   # 1728 tiles: 26 left over, split twice saves 12 steps
+    (1900, 2900, 1088),    # ragged tiles, 9 load steps: three splits save only 6
+    (1000, 4800, 1088),    # 76 tiles: 2 left over, split 9 ways = one load step per unit
+    (1024, 3072, 256),     # 48 tiles in one round: 2 load steps, nothing to gain
+])
+def test_pair_last_round_split_workspace_plan(m, n_out, k_red):
+    """The workspace query reports the CTA-pair kernel's last-round split scratch, computed
+    on the host without touching a GPU."""
+    size = ctypes.c_size_t(123)
+    lib = _lib.library()
+    assert lib.moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)) == _lib.MOSS_OK
+    assert size.value == _expected_pair_tail_bytes(m, n_out, k_red, _sm_count())

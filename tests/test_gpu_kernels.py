@@ -294,6 +294,105 @@ def test_split_k_without_workspace_matches(cuda_device):
     assert O.rel_fro(_np(y_split), _np(y_plain)) < 2e-3
 
 
+# ------------------------------------------------------------------ CTA-pair kernel: last-round split
+# Shapes whose last round of 256 x 256 tiles leaves SM pairs idle (148 SMs = 74 pairs). The
+# reduction lengths are short so the scalar fp64 oracle finishes in seconds.
+PAIR_TAIL_FWD = [
+    (768, 1088, 6400, 0),      # 75 tiles: 1 left over, split 9 ways = one load step per unit
+    (1000, 1088, 4800, 0),     # ragged M and N (76 tiles), 17 k-blocks: the last step holds one
+    (768, 1088, 6400, 32),     # fused LoRA term: its k-block lands in the last split
+]
+
+
+def _workspace_bytes(m, n_out, k_red):
+    size = ctypes.c_size_t()
+    _lib.check(_lib.library().moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)), "workspace")
+    return size.value
+
+
+def _skip_unless_148_sms(device):
+    if torch.cuda.get_device_properties(device).multi_processor_count != 148:
+        pytest.skip("the split plans of these shapes assume 148 SMs")
+
+
+@pytest.mark.parametrize("m,k,n,rank", PAIR_TAIL_FWD)
+def test_pair_last_round_split_forward_matches_oracle(cuda_device, m, k, n, rank):
+    """The tiles of the last round are split along K: f32 partials in the workspace, reduced
+    in split order by the last unit of each 32-row slice. Deterministic, within the oracle
+    bound, and equal to the unsplit kernel (no workspace) up to f32 summation order."""
+    _skip_unless_148_sms(cuda_device)
+    assert _workspace_bytes(m, n, k) > 0
+    x, q, s = _rand_problem(m, k, n, seed=m + 3 * k + n)
+    gen = torch.Generator().manual_seed(rank + 5)
+    bias = torch.randn(n, generator=gen) * 0.5
+    xd = x.to(cuda_device, torch.bfloat16)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    bd = bias.to(cuda_device, torch.bfloat16)
+    lora, extra = {}, {}
+    if rank:
+        xa = torch.randn(m, rank, generator=gen).to(torch.bfloat16)
+        lb = torch.randn(n, rank, generator=gen) * 0.05
+        lora = dict(lora_xa=xa.to(cuda_device), lora_b=lb.to(cuda_device), lora_scale=0.5)
+        extra = dict(lora_xa=_np(xa), lora_b=O.round_bf16(lb.numpy() * np.float32(0.5)), lora_scale=1.0)
+    y = qk.int8_linear_forward(xd, qd, sd, bd, torch.bfloat16, torch.bfloat16, **lora)
+    y2 = qk.int8_linear_forward(xd, qd, sd, bd, torch.bfloat16, torch.bfloat16, **lora)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(y, y2), "the split reduction must be deterministic"
+    expected = O.gemm_fwd(_np(x.to(torch.bfloat16)), q, s, w_kind=O.BF16, v_kind=O.BF16,
+                          bias=_np(bias.to(torch.bfloat16)), **extra)
+    _check_close(_np(y), expected, O.BF16)
+    if not rank:
+        y_whole = torch.empty_like(y)
+        rc = _lib.library().moss_w8a16_gemm_fwd(
+            xd.data_ptr(), 1, m, k, qd.data_ptr(), sd.data_ptr(), 1, n, bd.data_ptr(), 1, None, None, 0, 0, 1.0,
+            y_whole.data_ptr(), 1, None, 0, qk.status_buffer(cuda_device).data_ptr(),
+            torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc, "gemm")
+        torch.cuda.synchronize()
+        assert O.rel_fro(_np(y), _np(y_whole)) < 1e-3
+        assert (y == y_whole).float().mean().item() > 0.9
+
+
+def test_pair_last_round_split_grad_input_matches_oracle(cuda_device):
+    """Grad-input whose [768, 6400] output is 75 tiles: the last one is split 9 ways."""
+    _skip_unless_148_sms(cuda_device)
+    m, k, n = 768, 6400, 1088
+    assert _workspace_bytes(m, k, n) > 0
+    _, q, s = _rand_problem(1, k, n, seed=31)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    dy = torch.randn(m, n, generator=torch.Generator().manual_seed(32)).to(torch.bfloat16)
+    dx = qk.int8_linear_backward(dy.to(cuda_device), qd, sd, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)
+    dx2 = qk.int8_linear_backward(dy.to(cuda_device), qd, sd, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    assert torch.equal(dx, dx2)
+    _check_close(_np(dx), O.gemm_dx(_np(dy), q, s, w_kind=O.BF16, v_kind=O.BF16), O.BF16)
+
+
+def test_pair_last_round_split_long_reduction_against_torch_fp32(cuda_device):
+    """The config-5 grad-input of the (3072, 18432) projection at 2048 rows: 144 load steps
+    per tile, too long for the scalar oracle, so the reference is a torch fp32 matmul (TF32
+    off) on the oracle-decoded weight."""
+    _skip_unless_148_sms(cuda_device)
+    m, k, n = 2048, 3072, 18432
+    assert _workspace_bytes(m, k, n) > 0
+    _, q, s = _rand_problem(1, k, n, seed=41)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    dy = torch.randn(m, n, generator=torch.Generator().manual_seed(42)).to(torch.bfloat16).to(cuda_device)
+    dx = qk.int8_linear_backward(dy, qd, sd, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)
+    w = torch.from_numpy(O.dequantize(q, s, O.BF16)).to(cuda_device, torch.float32)
+    allow = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = dy.float() @ w
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = allow
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _check_close(_np(dx), ref.cpu().double().numpy(), O.BF16)
+
+
 # ------------------------------------------------------------------ few-row (operand-swapped) kernel
 FEW_ROWS = [
     (1, 3072, 3072),     # one token: 24 feature tiles, split over K
