@@ -141,7 +141,8 @@ def _compute_kind(dtype: torch.dtype) -> int:
 
 
 def _workspace(m: int, n_out: int, k_red: int, device: torch.device) -> tuple[torch.Tensor | None, int | None, int]:
-    """Scratch for split-K small-M launches from torch's caching allocator.
+    """Scratch for split launches from torch's caching allocator: small-M split-K, and the
+    CTA-pair kernel's split of a partly empty last round of tiles.
 
     Returns (owner tensor, 256-byte aligned address, bytes); the caller keeps the owner alive
     until the launch is enqueued (later reuse is ordered by the stream).
