@@ -31,6 +31,9 @@ def _ulp(t: torch.Tensor) -> torch.Tensor:
 CASES = [  # rows, dim, x dtype, weight dtype
     (4099, 128, torch.bfloat16, torch.bfloat16),   # per-head q/k norm (4 lanes per row)
     (300, 3072, torch.bfloat16, torch.bfloat16),   # block norm (one CTA per row)
+    (5000, 3072, torch.bfloat16, torch.bfloat16),  # more rows than resident CTAs: next row prefetched
+    (3000, 2048, torch.float16, torch.float16),    # two chunks per thread, prefetched
+    (2000, 4096, torch.float32, torch.float32),    # f32 rows, four chunks per thread
     (257, 64, torch.float16, torch.float16),       # 2 lanes per row
     (129, 24, torch.bfloat16, torch.bfloat16),     # 1 lane per row
     (41, 1024, torch.bfloat16, torch.bfloat16),    # a full warp per row
