@@ -370,6 +370,56 @@ def test_pair_last_round_split_grad_input_matches_oracle(cuda_device):
     _check_close(_np(dx), O.gemm_dx(_np(dy), q, s, w_kind=O.BF16, v_kind=O.BF16), O.BF16)
 
 
+def test_pair_last_round_split_f16_f32_output_and_lora_grad_input(cuda_device):
+    """The split path's reduction kernel with an f16 compute type, with an f32 output buffer
+    after the generic decode (f32 module dtype), and a grad-input whose LoRA block lands in
+    the last split. 768 x 6400 outputs are 75 tiles: the last one is split 9 ways."""
+    _skip_unless_148_sms(cuda_device)
+    m, k, n = 768, 1088, 6400
+    x, q, s = _rand_problem(m, k, n, seed=51)
+    qd, sd = torch.from_numpy(q).to(cuda_device), torch.from_numpy(s).to(cuda_device)
+    gen = torch.Generator().manual_seed(52)
+    bias = torch.randn(n, generator=gen) * 0.5
+    # f16 compute
+    y16 = qk.int8_linear_forward(x.to(cuda_device, torch.float16), qd, sd, bias.to(cuda_device, torch.float16),
+                                 torch.float16, torch.float16)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _check_close(_np(y16), O.gemm_fwd(_np(x.to(torch.float16)), q, s, w_kind=O.F16, v_kind=O.F16,
+                                      bias=_np(bias.to(torch.float16))), O.F16)
+    # f32 output, f32 module dtype (generic decode), through the C ABI with the workspace
+    xd = x.to(cuda_device, torch.bfloat16)
+    y32 = torch.empty(m, n, dtype=torch.float32, device=cuda_device)
+    owner, ws, ws_bytes = qk._workspace(m, n, k, cuda_device)
+    assert ws_bytes > 0
+    rc = _lib.library().moss_w8a16_gemm_fwd(
+        xd.data_ptr(), 1, m, k, qd.data_ptr(), sd.data_ptr(), 2, n, None, 0, None, None, 0, 0, 1.0,
+        y32.data_ptr(), 2, ws, ws_bytes, qk.status_buffer(cuda_device).data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
+    _lib.check(rc, "gemm")
+    torch.cuda.synchronize()
+    del owner
+    _status_ok(cuda_device)
+    _check_close(y32.cpu().numpy(), O.gemm_fwd(_np(xd), q, s, w_kind=O.F32, v_kind=O.BF16), O.BF16)
+    # grad-input [768, 6400] with the adapter term: the LoRA block is the last split's
+    md, kd, nd = 768, 6400, 1088
+    _, q2, s2 = _rand_problem(1, kd, nd, seed=53)
+    q2d, s2d = torch.from_numpy(q2).to(cuda_device), torch.from_numpy(s2).to(cuda_device)
+    assert _workspace_bytes(md, kd, nd) > 0
+    rank, scale = 32, 0.5
+    dy = torch.randn(md, nd, generator=gen).to(torch.bfloat16)
+    dyb = torch.randn(md, rank, generator=gen).to(torch.bfloat16)
+    la = torch.randn(rank, kd, generator=gen) * 0.05
+    dx = qk.int8_linear_backward(dy.to(cuda_device), q2d, s2d, torch.Size((md, kd)), torch.bfloat16, torch.bfloat16,
+                                 lora_dyb=dyb.to(cuda_device), lora_a=la.to(cuda_device), lora_scale=scale)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    a_eff = O.round_bf16(la.numpy() * np.float32(scale))
+    expected = O.gemm_dx(_np(dy), q2, s2, w_kind=O.BF16, v_kind=O.BF16, lora_dyb=_np(dyb), lora_a=a_eff,
+                         lora_scale=1.0)
+    _check_close(_np(dx), expected, O.BF16)
+
+
 def test_pair_last_round_split_long_reduction_against_torch_fp32(cuda_device):
     """The config-5 grad-input of the (3072, 18432) projection at 2048 rows: 144 load steps
     per tile, too long for the scalar oracle, so the reference is a torch fp32 matmul (TF32
