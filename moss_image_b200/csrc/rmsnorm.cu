@@ -250,8 +250,9 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(NormArgs a) {
   }
 }
 
-// Holds x and dy between the passes; the next rows' x and dy are loaded while the current
-// ones are reduced and written.
+// Holds x and dy between the passes. Unlike the forward it does not load the next rows ahead:
+// holding both rows of both tensors took 97 registers (2 CTAs per SM), and without it the
+// kernel uses 64 and is faster (221184 x 128: 49.1 -> 45.2 us).
 template <int KX, int KW, int L, int C>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
   constexpr int KY = promote(KX, KW);
@@ -264,17 +265,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kNormThreads / 32 * G;
   const int chunks = static_cast<int>(a.dim / 8);
   const float inv_dim = 1.0f / static_cast<float>(a.dim);
-  Chunk<KX> nx[C];
-  Chunk<KY> ndy[C];
   int64_t first = warp * G;
-#pragma unroll
-  for (int i = 0; i < C; ++i) {
-    const int c = lane + i * L;
-    if (first + g < a.rows && c < chunks) {
-      nx[i] = ldc<KX>(a.x, (first + g) * a.dim + c * 8);
-      ndy[i] = ldc<KY>(a.dy, (first + g) * a.dim + c * 8);
-    }
-  }
   for (; first < a.rows; first += stride) {
     const int64_t row = first + g;
     const bool live = row < a.rows;
@@ -284,16 +275,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(NormArgs a) {
     Chunk<KY> hdy[C];
 #pragma unroll
     for (int i = 0; i < C; ++i) {
-      hx[i] = nx[i];
-      hdy[i] = ndy[i];
-    }
-    const int64_t ahead = row + stride;
-#pragma unroll
-    for (int i = 0; i < C; ++i) {
       const int c = lane + i * L;
-      if (ahead < a.rows && c < chunks) {
-        nx[i] = ldc<KX>(a.x, ahead * a.dim + c * 8);
-        ndy[i] = ldc<KY>(a.dy, ahead * a.dim + c * 8);
+      if (live && c < chunks) {
+        hx[i] = ldc<KX>(a.x, base + c * 8);
+        hdy[i] = ldc<KY>(a.dy, base + c * 8);
       }
     }
     float dot = 0.f;
