@@ -114,3 +114,24 @@ def test_pair_last_round_split_workspace_plan(m, n_out, k_red):
     lib = _lib.library()
     assert lib.moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)) == _lib.MOSS_OK
     assert size.value == _expected_pair_tail_bytes(m, n_out, k_red, _sm_count())
+
+
+def test_pair_last_round_split_plan_matches_its_restatement_on_random_shapes():
+    """Random CTA-pair shapes (more than 128 rows, enough tiles to fill half the SMs): the
+    library's workspace query equals the restated plan for every one."""
+    import random
+
+    rng = random.Random(7)
+    lib = _lib.library()
+    sms = _sm_count()
+    checked = 0
+    while checked < 400:
+        m = rng.randint(129, 40000)
+        n_out = rng.randint(1, 24000)
+        k_red = 64 * rng.randint(1, 400)
+        if -(-m // 256) * -(-n_out // 256) * 4 < sms:
+            continue  # too few pair tiles: another kernel serves it
+        size = ctypes.c_size_t(123)
+        assert lib.moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)) == _lib.MOSS_OK
+        assert size.value == _expected_pair_tail_bytes(m, n_out, k_red, sms), (m, n_out, k_red)
+        checked += 1
