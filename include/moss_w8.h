@@ -62,6 +62,29 @@ MOSS_API int moss_version(void);
 MOSS_API const char* moss_last_error(void);
 
 /*
+ * Host-visible copy of the GEMM failure bits, so that a host can notice a failed launch
+ * without synchronising the device. The first call on a device (with that device current)
+ * allocates one word of mapped, portable pinned host memory for it; later calls return the
+ * same word. From then on every GEMM launched on that device that sets MOSS_STATUS_* bits in
+ * its `status` word also ORs them into this host word (a plain store over the host link, only
+ * on the failure path). The caller reads and clears it through *host_word.
+ * New in this library: the reference surfaces no device-side failures
+ * (training/quant_kernels.py:294-373 launch Triton kernels without a status channel).
+ */
+MOSS_API int moss_status_mirror(int** host_word);
+
+/*
+ * Test hook for the failure path: the next GEMM call from this host thread, if it runs the
+ * operand-swapped (few-row) kernel, makes that kernel's MMA issuer wait on a barrier that
+ * nothing arrives on. The wait is bounded (about two seconds), so the kernel then sets
+ * MOSS_STATUS_TIMEOUT_MMA, every role leaves its loop, the copies and MMAs in flight are
+ * drained, TMEM is freed and the launch returns with a garbage result; the context stays
+ * usable. Other kernels ignore the request; it is consumed by the next GEMM call either way.
+ * New in this library (no counterpart in the reference).
+ */
+MOSS_API int moss_debug_stall_next_gemm(void);
+
+/*
  * Per-output-channel symmetric int8 quantiser.
  * Replaces the quantiser in FrozenInt8Linear.__init__ (training/quantization.py:87-91):
  *   s[n] = max_k |float(w[n,k])| / 127 (IEEE f32 division); s[n] = 1 where it is 0;
@@ -131,6 +154,11 @@ MOSS_API int moss_w8a16_gemm_fwd(const void* x, int x_dtype, int64_t m, int64_t 
  *   - The first call on a device, with that device current, looks up the array's device
  *     address (cudaGetSymbolAddress) and caches it; make that first call before any stream
  *     capture.
+ *   - The array's memory is committed when the library's device code is loaded on a device.
+ *     Under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default) that is this first
+ *     call, or the first launch of any of this library's kernels there, and it can then fail
+ *     with an out-of-memory error if another pool has already reserved the free memory. Make
+ *     the first call at start-up, before such a pool grows, or set CUDA_MODULE_LOADING=EAGER.
  *   - Small-M problems whose moss_w8a16_gemm_workspace_bytes(m, n, k) exceeds the array are
  *     refused with MOSS_ERR_INVALID_ARGUMENT before any launch; use moss_w8a16_gemm_fwd for
  *     them. CTA-pair problems whose last-round split would not fit run without that split.

@@ -40,6 +40,8 @@ _sz = ctypes.c_size_t
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "moss_version": (_i32, []),
     "moss_last_error": (ctypes.c_char_p, []),
+    "moss_status_mirror": (_i32, [ctypes.POINTER(ctypes.POINTER(ctypes.c_int))]),
+    "moss_debug_stall_next_gemm": (_i32, []),
     "moss_w8_quantize": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_w8_dequantize": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp, _vp]),
     "moss_w8a16_gemm_workspace_bytes": (_i32, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),

@@ -24,7 +24,7 @@ from .quant_kernels import (
     hadamard_transform,
     validate_quantized_backend,
 )
-from .quantization import FrozenInt8Linear
+from .quantization import FrozenInt8Linear, replace_frozen_linears
 
 
 def effective_group_size(in_features: int, group_size: int = 256) -> int:
@@ -165,14 +165,4 @@ def quantize_frozen_convrot_linears(model: nn.Module, group_size: int = 256, *, 
     """
     effective_group_size(1, group_size)  # validate even when nothing is replaced
     validate_quantized_backend(backend)
-    names = []
-    for name, child in list(model.named_modules()):
-        if not name or not isinstance(child, nn.Linear):
-            continue
-        if any(parameter.requires_grad for parameter in child.parameters()):
-            continue
-        parent_name, _, leaf = name.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        setattr(parent, leaf, FrozenConvRotLinear(child, group_size, backend=backend))
-        names.append(name)
-    return names
+    return replace_frozen_linears(model, lambda linear: FrozenConvRotLinear(linear, group_size, backend=backend))

@@ -36,6 +36,24 @@ __device__ __forceinline__ void report_status(int* status, int code) {
   if (status != nullptr) atomicOr(status, code);
 }
 
+// Where a GEMM launch reports a failure: the caller's device status word (OR-ed atomically),
+// and optionally a host-visible copy in mapped pinned host memory (moss_status_mirror) that
+// the host reads without synchronising the device. Only failure paths write either word.
+// The copy is a plain read-modify-write over the host link (no atomics to host memory): a
+// concurrent report can lose another's bit, never the fact that a report happened.
+struct StatusSink {
+  int* dev;
+  int* host;
+};
+__device__ __forceinline__ void report_status(StatusSink s, int code) {
+  if (s.dev != nullptr) atomicOr(s.dev, code);
+  if (s.host != nullptr) {
+    volatile int* h = s.host;
+    *h = *h | code;
+    __threadfence_system();
+  }
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -66,7 +84,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // flag plus `code` in the device status word) when the budget runs out or another role
 // has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+                                          StatusSink status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
@@ -222,7 +240,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 // Bounded wait on a barrier that receives arrivals from the peer CTA.
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* status, int code) {
+                                                  StatusSink status, int code) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
@@ -236,6 +254,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// Store a 32-bit value into the shared memory of another CTA of the cluster (mapa address).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t value) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(value) : "memory");
+}
 
 // Tiled 2-D TMA load into this CTA's shared memory whose completion is signalled on the
 // mbarrier at `bar_cluster` (a shared::cluster address; here the pair leader's barrier).

@@ -14,6 +14,14 @@ namespace moss {
 
 std::string& last_error_slot();
 
+// Device-visible address of the current device's host-visible status copy (set up by
+// moss_status_mirror), or nullptr when the caller has not asked for one.
+int* status_mirror_for_current_device();
+
+// Whether the calling thread asked for a debug stall of its next GEMM
+// (moss_debug_stall_next_gemm); the request is consumed by this call.
+bool take_debug_stall();
+
 inline int fail(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;

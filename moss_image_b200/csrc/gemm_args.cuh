@@ -23,7 +23,10 @@ struct Args {
   const void* ext_a; int64_t ld_ext_a;             // LoRA: [M, r] (value dtype)
   const void* ext_b; int ext_b_kind; int64_t ld_ext_b; int ext_r;  // fwd [Nc, r]; dx [r, Nc]
   float ext_scale;
-  int* status;
+  StatusSink status;        // failure bits: the caller's device word (+ the host-visible copy)
+  // Test hook (moss_debug_stall_next_gemm): the operand-swapped kernel's MMA issuer waits on a
+  // barrier nothing arrives on, so its bounded wait runs out; 0 in every ordinary launch.
+  int debug_stall;
   // split-K (1-CTA kernel): work units are (tile, split); split s covers weight k-blocks
   // [s * kb_per_split, (s + 1) * kb_per_split) and the last split also the LoRA blocks.
   // Partial f32 tiles go to `partial` [splits][M][Nc]; `counters` [tiles] count arrivals.

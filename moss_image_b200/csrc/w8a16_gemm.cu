@@ -654,7 +654,8 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.ld_ext_b = dx ? Nc : ext_r;
   a.ext_r = ext_a ? static_cast<int>(ext_r) : 0;
   a.ext_scale = ext_scale;
-  a.status = status;
+  a.status = StatusSink{status, status_mirror_for_current_device()};
+  a.debug_stall = take_debug_stall() ? 1 : 0;
   a.splits = 1;
   a.kb_per_split = a.main_kb;
   a.partial = nullptr;

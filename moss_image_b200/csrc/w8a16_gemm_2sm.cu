@@ -64,6 +64,13 @@ constexpr uint32_t kSmemBytes = kDataBytes + 1024 + 512;
 constexpr int64_t kMaxTailSplits = 16;
 constexpr int64_t kMinTailGainSteps = 8;
 static_assert(kSmemBytes <= 227 * 1024, "rings exceed the 227 KB of shared memory a CTA may use");
+// Budget of the final wait for the peer CTA. Every other wait of either CTA is bounded: after
+// a failure a role gives up its pipeline wait within kWaitBudgetCycles (or at once, when the
+// abort flag is raised), and the drains of its own copies and MMAs take at most kAStages more
+// budgets. The peer therefore reaches the exit barrier within about 4 budgets of any failure,
+// and this wait outlasts that by a factor of two: a CTA that gives up here has a peer that can
+// no longer run at all, so freeing TMEM cannot race the peer's MMAs or remote arrivals.
+constexpr long long kExitBudgetCycles = 8 * kWaitBudgetCycles;
 
 // Load schedule of one tile: main steps of up to kSub weight k-blocks, then one step per
 // LoRA k-block. Every role walks the same sequence. Tiles in flight at the same time walk K
@@ -649,10 +656,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
+    // A failure in this CTA ends the peer's loops too (it would otherwise wait out its own
+    // budgets on barriers this CTA no longer feeds). The peer is still resident: it cannot
+    // pass its exit wait before the arrival below.
+    if (*abort_flag) st_shared_cluster_u32(mapa_shared(smem_u32(&bars->abort_flag), rank ^ 1u), 1u);
     mbar_arrive_cluster(mapa_shared(bar(bars->exit_bar), rank ^ 1u));
     const long long start = clock64();
     while (!mbar_try_wait_cluster(bar(bars->exit_bar), 0)) {
-      if (clock64() - start > kWaitBudgetCycles) {
+      if (clock64() - start > kExitBudgetCycles) {
         report_status(args.status, MOSS_STATUS_TIMEOUT_DRAIN);
         break;
       }

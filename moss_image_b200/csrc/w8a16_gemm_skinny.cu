@@ -257,6 +257,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     bool ok = true;
     bool issued_any = false;
+    if (args.debug_stall) {
+      // Test hook (moss_debug_stall_next_gemm): nothing arrives on the drain barrier before an
+      // MMA is issued, so this bounded wait runs out, raises the abort flag and reports
+      // MOSS_STATUS_TIMEOUT_MMA; every role then leaves and the copies in flight are drained.
+      mbar_wait(bar(bars->drain), 0, abort_flag, args.status, MOSS_STATUS_TIMEOUT_MMA);
+      ok = false;
+    }
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
       const Unit U = unit_of(args, u);
       const int acc = it & 1;

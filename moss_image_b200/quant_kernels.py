@@ -1,14 +1,23 @@
 """Backend selection, validation and launchers for the sm_100a weight-only int8 linear.
 
 Mirrors the host interface of ``training/quant_kernels.py`` (backend strings, validation
-messages, autocast dtype rule, ``out=`` buffers) so callers of the reference switch
-without edits. Differences, by design:
+messages and exception types, autocast dtype rule, ``out=`` buffers) so callers of the
+reference switch without edits. The error texts are the reference's own, including the
+"Triton quantized backend is unavailable: <reason>." prefix of its explicit-backend check
+(training/quant_kernels.py:78), so code and tests that match on them keep working.
 
-* every accepted backend string (``auto``, ``eager``, ``triton``) executes the B200
-  tcgen05 kernels of ``libmoss_w8.so`` on CUDA tensors; there is no Triton and no CPU
-  fallback - CPU tensors raise ``RuntimeError``;
-* the compute dtype must be float16 or bfloat16 (the tcgen05 ``kind::f16`` path); a
-  float32 compute dtype raises ``RuntimeError`` with a message saying so.
+Deliberate differences, all of them refusals where the reference would compute on another
+device or in another precision (there is no CPU and no eager fallback):
+
+* every accepted backend string (``auto``, ``eager``, ``triton``) executes the sm_100a
+  kernels of ``libmoss_w8.so``; where the reference resolves ``auto``/``eager`` to its
+  dense-decode path (training/quant_kernels.py:64-79), an input the kernels cannot run
+  raises ``RuntimeError`` with the reference's message - CPU tensors included;
+* the compute dtype must be float16 or bfloat16 (tcgen05 ``kind::f16``); a float32
+  compute dtype (an fp32 module outside autocast) raises ``RuntimeError``. The trainer never
+  reaches it on CUDA: LoRA mode casts the model to bfloat16 (training/train.py:579-580);
+* non-contiguous inputs and empty matrices, which the reference's Triton launcher refuses
+  (training/quant_kernels.py:58-61), are accepted (copied contiguous / shaped results).
 """
 
 from __future__ import annotations
@@ -24,7 +33,13 @@ QuantizedBackend = Literal["auto", "eager", "triton"]
 
 _BACKENDS = {"auto", "eager", "triton"}
 
+# Prefix of every "cannot run this here" error (the reference's text, training/quant_kernels.py:78).
+UNAVAILABLE = "Triton quantized backend is unavailable"
+
 _status_buffers: dict[tuple[str, int | None], torch.Tensor] = {}
+# host-visible copies of the status bits (moss_status_mirror), by device index
+_status_mirrors: dict[int, "ctypes._Pointer"] = {}
+_backward_polls: set[int] = set()
 
 # Optional launch observer (benchmarks): called as observer(kind, m, n, k, device) before a
 # GEMM launch and returns a callable invoked right after it.
@@ -59,7 +74,7 @@ def _unsupported_reason(tokens: torch.Tensor, weight: torch.Tensor, scale: torch
         try:
             _lib.library()
         except RuntimeError as error:
-            return f"the CUDA library is unavailable ({error})"
+            return f"the sm_100a kernel library is not installed ({error})"
     if tokens.device.type != "cuda":
         return "the input is not on CUDA"
     if weight.device != tokens.device or scale.device != tokens.device:
@@ -83,14 +98,14 @@ def resolve_quantized_backend(
 ) -> QuantizedBackend:
     """Validate the backend string and that the sm_100a kernels can run these tensors.
 
-    Reference: training/quant_kernels.py:64-79. Unlike the reference, ``auto`` and
-    ``eager`` do not fall back to a CPU or dequantise-then-cuBLAS path: an input the
-    kernels cannot run raises ``RuntimeError``.
+    Reference: training/quant_kernels.py:64-79, with its message. Unlike the reference,
+    ``auto`` and ``eager`` do not fall back to a CPU or dequantise-then-cuBLAS path: an
+    input the kernels cannot run raises ``RuntimeError`` for every backend string.
     """
     selected = validate_quantized_backend(backend)
     reason = _unsupported_reason(tokens, weight, scale)
     if reason is not None:
-        raise RuntimeError(f"int8 quantized backend is unavailable: {reason}.")
+        raise RuntimeError(f"{UNAVAILABLE}: {reason}.")
     return selected
 
 
@@ -106,14 +121,52 @@ def autocast_compute_dtype(tokens: torch.Tensor, module_dtype: torch.dtype) -> t
     return torch.get_autocast_dtype("cuda")
 
 
+def _device_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 def status_buffer(device: torch.device) -> torch.Tensor:
-    """Per-device int32 word the kernels OR their MOSS_STATUS_* bits into."""
-    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    """Per-device int32 word the kernels OR their MOSS_STATUS_* bits into.
+
+    Creating it also sets up the device's host-visible copy of those bits
+    (``moss_status_mirror``), which ``poll_device_status`` reads without a device sync.
+    """
+    key = ("cuda", _device_index(device))
     buf = _status_buffers.get(key)
     if buf is None:
-        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key[1]))
+        dev = torch.device("cuda", key[1])
+        buf = torch.zeros(1, dtype=torch.int32, device=dev)
+        word = ctypes.POINTER(ctypes.c_int)()
+        with torch.cuda.device(dev):
+            _lib.check(_lib.library().moss_status_mirror(ctypes.byref(word)), "moss_status_mirror")
+        _status_mirrors[key[1]] = word
         _status_buffers[key] = buf
     return buf
+
+
+def poll_device_status(device: torch.device) -> int:
+    """Raise if a kernel on ``device`` has reported a pipeline timeout; never synchronises.
+
+    Reads the host-visible copy of the status bits, which a failed launch writes when it
+    completes. The failure is sticky: every later GEMM call on the device raises until
+    ``check_device_status`` (or ``reset_device_status``) clears it.
+    """
+    word = _status_mirrors.get(_device_index(device))
+    value = 0 if word is None else int(word[0])
+    if value & _lib.STATUS_TIMEOUT_MASK:
+        raise RuntimeError(f"sm_100a int8 kernel reported a pipeline timeout (status 0x{value:x}); its output "
+                           "is invalid. Clear with quant_kernels.reset_device_status() after handling it.")
+    return value
+
+
+def reset_device_status(device: torch.device) -> None:
+    """Clear the device status word and its host-visible copy."""
+    buf = status_buffer(device)
+    buf.zero_()
+    torch.cuda.synchronize(buf.device)
+    word = _status_mirrors.get(_device_index(device))
+    if word is not None:
+        word[0] = 0
 
 
 def check_device_status(device: torch.device | None = None, *, reset: bool = True) -> int:
@@ -123,18 +176,38 @@ def check_device_status(device: torch.device | None = None, *, reset: bool = Tru
     for dev in devices:
         buf = status_buffer(dev)
         value = int(buf.item())
+        word = _status_mirrors.get(_device_index(dev))
+        if word is not None:
+            value |= int(word[0])
         if reset and value:
-            buf.zero_()
+            reset_device_status(dev)
         worst |= value
     if worst & _lib.STATUS_TIMEOUT_MASK:
         raise RuntimeError(f"sm_100a int8 kernel reported a pipeline timeout (status 0x{worst:x}).")
     return worst
 
 
+def _poll_after_backward(device: torch.device) -> None:
+    """Queue a status poll for the end of the running backward pass (once per pass)."""
+    index = _device_index(device)
+    if index in _backward_polls:
+        return
+    _backward_polls.add(index)
+
+    def _poll() -> None:
+        _backward_polls.discard(index)
+        poll_device_status(torch.device("cuda", index))
+
+    try:
+        torch.autograd.Variable._execution_engine.queue_callback(_poll)
+    except RuntimeError:  # not inside a backward pass (direct launcher call)
+        _backward_polls.discard(index)
+
+
 def _compute_kind(dtype: torch.dtype) -> int:
     if dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError(
-            f"int8 quantized backend is unavailable: compute dtype {dtype} is unsupported "
+            f"{UNAVAILABLE}: compute dtype {dtype} is unsupported "
             "(the sm_100a kernels compute in float16 or bfloat16; use autocast or a half-precision module)."
         )
     return _lib.DTYPE_CODES[dtype]
@@ -183,6 +256,9 @@ def int8_linear_forward(
     reference's kernel casts its tile loads) and made contiguous if needed.
     """
     v_kind = _compute_kind(output_dtype)
+    if tokens.is_cuda:
+        status_buffer(tokens.device)
+        poll_device_status(tokens.device)
     matrix = _matrix_view(tokens)
     if matrix.dtype != output_dtype:
         matrix = matrix.to(output_dtype)
@@ -195,9 +271,9 @@ def int8_linear_forward(
     else:
         output = out.reshape(rows, out_features)
         if output.dtype != output_dtype or not output.is_contiguous():
-            raise ValueError("int8 output buffer has the wrong dtype or is not contiguous.")
+            raise ValueError("Triton output buffer has the wrong dtype or is not contiguous.")
     if bias is not None and (bias.device != tokens.device or not bias.is_contiguous()):
-        raise RuntimeError("int8 quantized bias must be contiguous and on the input device.")
+        raise RuntimeError("Triton quantized bias must be contiguous and on the input device.")
     rank = 0
     if lora_xa is not None:
         if lora_b is None:
@@ -251,6 +327,10 @@ def int8_linear_backward(
     """
     compute_dtype = gradient.dtype if compute_dtype is None else compute_dtype
     v_kind = _compute_kind(compute_dtype)
+    if gradient.is_cuda:
+        status_buffer(gradient.device)
+        poll_device_status(gradient.device)
+        _poll_after_backward(gradient.device)
     matrix = _matrix_view(gradient)
     if matrix.dtype != compute_dtype:
         matrix = matrix.to(compute_dtype)
@@ -263,7 +343,7 @@ def int8_linear_backward(
     else:
         grad_input = out.reshape(rows, in_features)
         if grad_input.dtype != input_dtype or not grad_input.is_contiguous():
-            raise ValueError("int8 input-gradient buffer has the wrong dtype or is not contiguous.")
+            raise ValueError("Triton input-gradient buffer has the wrong dtype or is not contiguous.")
     rank = 0
     if lora_dyb is not None:
         if lora_a is None:
@@ -337,7 +417,7 @@ def quantize_weight(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def dequantize_weight(weight: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """Transient decoded weight ``round_d(q * round_d(s))`` (reference quantization.py:23-24)."""
     if weight.device.type != "cuda":
-        raise RuntimeError("int8 quantized backend is unavailable: the weight is not on CUDA.")
+        raise RuntimeError(f"{UNAVAILABLE}: the weight is not on CUDA.")
     out = torch.empty(weight.shape, dtype=dtype, device=weight.device)
     rc = _lib.library().moss_w8_dequantize(
         _lib.ptr(weight), _lib.ptr(scale), weight.shape[0], weight.shape[1], _lib.dtype_code(dtype),
@@ -375,7 +455,7 @@ def hadamard_transform(
     if out.shape != tokens.shape or out.dtype != tokens.dtype or not out.is_contiguous():
         raise ValueError("Triton Hadamard output must match its contiguous input.")
     if tokens.device.type != "cuda":
-        raise RuntimeError("int8 quantized backend is unavailable: the input is not on CUDA.")
+        raise RuntimeError(f"{UNAVAILABLE}: the input is not on CUDA.")
     rc = _lib.library().moss_hadamard_rotate(
         _lib.ptr(tokens), _lib.dtype_code(tokens.dtype), tokens.shape[0], tokens.shape[1], int(group_size),
         _lib.ptr(out), _lib.stream_handle(tokens.device),

@@ -9,6 +9,8 @@ Neither direction materialises a floating-point copy of the weight.
 
 from __future__ import annotations
 
+from typing import Callable
+
 import torch
 from torch import nn
 
@@ -173,13 +175,14 @@ def configure_quantized_backend(model: nn.Module, backend: str) -> list[str]:
     return names
 
 
-def quantize_frozen_linears(model: nn.Module, *, backend: str = "eager") -> list[str]:
-    """Replace frozen Linear children, including bases inside existing LoRA wrappers.
+def replace_frozen_linears(model: nn.Module, make: Callable[[nn.Linear], nn.Module]) -> list[str]:
+    """Swap every frozen ``nn.Linear`` below ``model`` (including bases inside LoRA wrappers)
+    for ``make(linear)``; trainable linears are left alone. Returns the replaced paths.
 
-    Reference: training/quantization.py:145-162. Trainable linears are left alone.
-    Returns the replaced module paths.
+    The module walk shared by ``quantize_frozen_linears`` and
+    ``convrot.quantize_frozen_convrot_linears`` (reference training/quantization.py:152-162 and
+    training/convrot.py:163-172 walk the same way).
     """
-    validate_quantized_backend(backend)
     names = []
     for name, child in list(model.named_modules()):
         if not name or not isinstance(child, nn.Linear):
@@ -188,6 +191,16 @@ def quantize_frozen_linears(model: nn.Module, *, backend: str = "eager") -> list
             continue
         parent_name, _, leaf = name.rpartition(".")
         parent = model.get_submodule(parent_name) if parent_name else model
-        setattr(parent, leaf, FrozenInt8Linear(child, backend=backend))
+        setattr(parent, leaf, make(child))
         names.append(name)
     return names
+
+
+def quantize_frozen_linears(model: nn.Module, *, backend: str = "eager") -> list[str]:
+    """Replace frozen Linear children, including bases inside existing LoRA wrappers.
+
+    Reference: training/quantization.py:145-162. Trainable linears are left alone.
+    Returns the replaced module paths.
+    """
+    validate_quantized_backend(backend)
+    return replace_frozen_linears(model, lambda linear: FrozenInt8Linear(linear, backend=backend))
