@@ -58,6 +58,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
     p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--offload-pairs", type=int, default=2,
+                   help="alternated (offload off, offload on) arm pairs timed after the main region (0: none)")
+    p.add_argument("--offload-arm-steps", type=int, default=3)
     p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load",
                                         "segment_modulate", "segment_gate", "rmsnorm", "rmsnorm_bwd"], default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
@@ -65,6 +68,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--k", type=int, default=3072)
     p.add_argument("--n", type=int, default=3072)
     p.add_argument("--sweep", action="store_true")
+    p.add_argument("--sweep-m", default=None, help="comma-separated M values of the sweep (default: the config grid)")
     return p.parse_args()
 
 
@@ -218,21 +222,35 @@ def block_swap_summary(before: dict, after: dict, steps: int, elapsed_ms: float,
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_baseline_sample(reps: int = 1) -> dict:
+def cpu_baseline_sample(reps: int = 5, warmup: int = 2) -> dict:
+    """The reference's CPU algorithm on this host: one checkpointed block step on one sample
+    (median of `reps` after `warmup`), plus the single-linear configuration op by op."""
     sys.path.insert(0, str(REPO))
     from oracle import cpu_step
 
     seq = IMG_TOKENS + TXT_TOKENS
-    result = cpu_step.time_block_sample(dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seq=seq, reps=reps, warmup=1)
+    result = cpu_step.time_block_sample(dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seq=seq, reps=reps,
+                                        warmup=warmup)
     per_block = statistics.median(result["seconds"])
     value = seq / (per_block * DEPTH)  # tokens/s of the full 36-block step, per sample
+    ops = cpu_step.time_config1_ops(reps=reps, warmup=warmup)
     return {"value": value, "unit": "tokens/s", "cores": result["threads"], "kind": "port",
             "sample": (f"1 of {DEPTH} blocks x 1 sample ({seq} tokens), checkpointed fwd + recompute + bwd, "
-                       f"median of {reps} after 1 warm-up, extrapolated x{DEPTH}; cpu={cpu_step.cpu_model_name()}"),
-            "seconds_per_block_sample": per_block}
+                       f"median of {reps} after {warmup} warm-ups; value = {seq} tokens / ({DEPTH} x the block "
+                       f"time); cpu={cpu_step.cpu_model_name()}, os.cpu_count()={os.cpu_count()}"),
+            "seconds_per_block_sample": per_block, "extrapolated_x": DEPTH,
+            "config1_ops": ops}
 
 
 def run_reference(args: argparse.Namespace) -> None:
+    """The reference's CPU implementation of the step, on this host's cores.
+
+    Each timed step is a bounded sample of the workload: one of the 36 blocks on one of the
+    2 samples, run as gradient checkpointing runs it (no-grad forward, recompute forward,
+    backward). ``ms_per_step`` is that sample's measured time; ``value`` converts it to the
+    metric's tokens/s of a full step, which is ``extrapolated_x`` = 36 blocks x 2 samples
+    such samples long.
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -241,19 +259,30 @@ def run_reference(args: argparse.Namespace) -> None:
 
     seq = IMG_TOKENS + TXT_TOKENS
     steps = max(1, args.steps)
+    t0 = time.perf_counter()
     result = cpu_step.time_block_sample(dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seq=seq,
-                                        reps=steps, warmup=min(args.warmup, 1))
-    per_block = statistics.median(result["seconds"])
-    value = seq / (per_block * DEPTH)
+                                        reps=steps, warmup=args.warmup)
+    wall = time.perf_counter() - t0
+    per_sample = statistics.median(result["seconds"])
+    value = seq / (per_sample * DEPTH)
+    extrapolated = DEPTH * args.batch
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": per_block * DEPTH * args.batch * 1e3,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": per_sample * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "reference CPU path (oracle port) of the 36-block int8 LoRA step, batch 2 x 4608 tokens",
+        "config": {"workload": (f"reference CPU path (oracle port of the eager int8 LoRA block) on the "
+                                f"{DEPTH}-block step, batch {args.batch} x {seq} tokens; each timed step is a "
+                                f"bounded sample: 1 block x 1 sample"),
                    "global_batch": args.batch, "seq_len": seq, "parallelism": "cpu"},
+        "step_is_sample": True,
+        "extrapolated_x": extrapolated,
+        "full_step_ms_extrapolated": per_sample * extrapolated * 1e3,
+        "wall_s": wall,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": result["threads"], "kind": "port",
-                         "sample": f"each step: 1 of {DEPTH} blocks x 1 sample, checkpointed fwd + recompute + bwd, "
-                                   f"extrapolated x{DEPTH}; cpu={cpu_step.cpu_model_name()}"},
+                         "sample": (f"each step: 1 of {DEPTH} blocks x 1 of {args.batch} samples, checkpointed "
+                                    f"fwd + recompute + bwd, median of {steps} after {args.warmup} warm-ups; "
+                                    f"value = {seq} tokens / ({DEPTH} x the sample time); "
+                                    f"cpu={cpu_step.cpu_model_name()}")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -393,49 +422,130 @@ def run_kernel(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_sweep(args: argparse.Namespace) -> None:
+def graph_time_us(calls, device, reps: int | None = None) -> float:
+    """Device time per launch of back-to-back launches: every call in `calls` enqueues one
+    launch on the current stream; they are captured once in a CUDA graph (no host work between
+    launches) and the graph is replayed after warm-up, timed with CUDA events."""
     import torch
 
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for call in calls:  # one-time set-up (attributes, symbol lookups) outside the capture
+            call()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for call in calls:
+            call()
+    graph.replay()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if reps is None:
+        start.record()
+        graph.replay()
+        end.record()
+        end.synchronize()
+        once = max(start.elapsed_time(end), 1e-3)
+        reps = int(min(10, max(2, 30.0 / once)))
+    for _ in range(2):
+        graph.replay()
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    end.synchronize()
+    us = start.elapsed_time(end) * 1e3 / (reps * len(calls))
+    del graph
+    return us
+
+
+def run_sweep(args: argparse.Namespace) -> None:
+    """The W8A16 GEMM sweep (M x (K, N), forward and grad-input), one JSON line per shape.
+
+    Three implementations on the same GPU, each timed as back-to-back launches captured in a
+    CUDA graph (device time only, no host launch latency):
+    * ``ours``: this library's kernels through the C ABI, preallocated buffers and workspace;
+    * ``eager_gpu``: the reference's eager algorithm (decode ``q.to(bf16) * s.to(bf16)[:, None]``
+      then ``F.linear`` / ``matmul`` on cuBLAS, training/quantization.py:23-24,43,61-64);
+    * ``cublas_bf16``: a plain bf16 cuBLAS GEMM on a dense bf16 weight (the ceiling).
+    Every launch reads its own copy of the weight, with enough copies that the weights touched
+    by one graph exceed twice the 126 MB L2: the weight stream is measured from HBM.
+    """
+    import ctypes
+
+    import torch
+    import torch.nn.functional as F
+
+    from moss_image_b200 import _lib
     from moss_image_b200 import quant_kernels as qk
 
-    peaks, _ = measured_peaks()
+    peaks, peak_kind = measured_peaks()
     dev = torch.device("cuda", 0)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for kn in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072), (3072, 18432)]:
-        k, n = kn
+    torch.cuda.set_device(dev)
+    lib = _lib.library()
+    status = qk.status_buffer(dev)
+    l2_cover = 320 << 20
+    grid_m = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else [128, 512, 2048, 8192, 32768]
+    for k, n in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072), (3072, 18432)]:
+        copies = max(1, -(-l2_cover // (n * k)))
+        dense_copies = max(1, -(-l2_cover // (2 * n * k)))
         gen = torch.Generator(device=dev).manual_seed(0)
-        w = torch.randn(n, k, device=dev, generator=gen) * 0.02
-        q, s = qk.quantize_weight(w)
-        del w
-        for m in (128, 512, 2048, 8192, 32768):
-            x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
-            dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
-            res = {"m": m, "k": k, "n": n}
+        qs = [torch.randint(-127, 128, (n, k), generator=gen, device=dev, dtype=torch.int8) for _ in range(copies)]
+        ss = [torch.rand(n, generator=gen, device=dev) * 4e-4 + 1e-4 for _ in range(copies)]
+        dense = [(qs[i % copies].to(torch.bfloat16) * ss[i % copies].to(torch.bfloat16)[:, None])
+                 for i in range(dense_copies)]
+        for m in grid_m:
+            x = torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16)
+            dy = torch.randn(m, n, generator=gen, device=dev).to(torch.bfloat16)
+            y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+            dx = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+            res = {"m": m, "k": k, "n": n, "weight_copies": copies}
+            flops = 2.0 * m * n * k
             for kind in ("fwd", "dx"):
-                if kind == "fwd":
-                    fn = lambda: qk.int8_linear_forward(x, q, s, None, torch.bfloat16, torch.bfloat16)  # noqa: E731
-                else:
-                    fn = lambda: qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16,  # noqa: E731
-                                                         torch.bfloat16)
-                for _ in range(3):
-                    fn()
-                times = []
-                for _ in range(max(3, args.steps)):
-                    flush.zero_()  # evict L2 between timed launches
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record()
-                    fn()
-                    b.record()
-                    b.synchronize()
-                    times.append(a.elapsed_time(b))
-                ms = statistics.median(times)
-                flops = 2.0 * m * n * k
+                n_out, k_red = (n, k) if kind == "fwd" else (k, n)
+                size = ctypes.c_size_t()
+                _lib.check(lib.moss_w8a16_gemm_workspace_bytes(m, n_out, k_red, ctypes.byref(size)), "workspace")
+                ws_owner = torch.empty(size.value + 256, dtype=torch.uint8, device=dev)
+                ws = (ws_owner.data_ptr() + 255) // 256 * 256
+
+                def ours(i, kind=kind, size=size, ws=ws):
+                    stream = torch.cuda.current_stream(dev).cuda_stream
+                    if kind == "fwd":
+                        rc = lib.moss_w8a16_gemm_fwd(x.data_ptr(), 1, m, k, qs[i].data_ptr(), ss[i].data_ptr(), 1, n,
+                                                     None, 0, None, None, 0, 0, 1.0, y.data_ptr(), 1, ws, size.value,
+                                                     status.data_ptr(), stream)
+                    else:
+                        rc = lib.moss_w8a16_gemm_dx(dy.data_ptr(), 1, m, n, qs[i].data_ptr(), ss[i].data_ptr(), 1, k,
+                                                    None, None, 0, 0, 1.0, dx.data_ptr(), 1, ws, size.value,
+                                                    status.data_ptr(), stream)
+                    _lib.check(rc, "gemm")
+
+                def eager(i, kind=kind):
+                    w = qs[i].to(torch.bfloat16) * ss[i].to(torch.bfloat16)[:, None]
+                    return F.linear(x, w) if kind == "fwd" else dy.matmul(w)
+
+                def cublas(i, kind=kind):
+                    return F.linear(x, dense[i]) if kind == "fwd" else dy.matmul(dense[i])
+
                 nbytes = n * k + 4 * n + 2 * m * k + 2 * m * n
                 t_roof = max(flops / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9))
-                res[kind] = {"us": ms * 1e3, "tflops": flops / ms / 1e9, "gbs": nbytes / ms / 1e6,
-                             "roofline_frac": t_roof / (ms * 1e-3)}
-            del x, dy
+                entry = {}
+                for label, fn, count in (("ours", ours, copies), ("eager_gpu", eager, copies),
+                                         ("cublas_bf16", cublas, dense_copies)):
+                    us = graph_time_us([lambda i=i, fn=fn: fn(i) for i in range(count)], dev)
+                    entry[label] = {"us": us, "tflops": flops / us / 1e6}
+                entry["ours"].update({"gbs": nbytes / entry["ours"]["us"] / 1e3,
+                                      "roofline_frac": t_roof / (entry["ours"]["us"] * 1e-6)})
+                entry["speedup_vs_eager_gpu"] = entry["eager_gpu"]["us"] / entry["ours"]["us"]
+                entry["frac_of_cublas_bf16"] = entry["cublas_bf16"]["us"] / entry["ours"]["us"]
+                res[kind] = entry
+                del ws_owner
+            res["roofline_peaks"] = f"max(flops / bf16_tflops, bytes / hbm_gbs) ({peak_kind})"
+            del x, dy, y, dx
+            torch.cuda.empty_cache()
             print(json.dumps(res), flush=True)
+        del qs, ss, dense
+        torch.cuda.empty_cache()
     qk.check_device_status(dev)
 
 
@@ -535,7 +645,7 @@ def run_train(args: argparse.Namespace) -> None:
     model.activation_offload = not args.no_offload
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
-    reducer = GradAllReducer(params)
+    reducer = GradAllReducer(params, timing=True)
 
     img_tokens, txt_tokens = args.img_tokens, args.txt_tokens
     seq = img_tokens + txt_tokens
@@ -610,6 +720,66 @@ def run_train(args: argparse.Namespace) -> None:
     e2e_ms = e_start.elapsed_time(e_end)
     qk.check_device_status(dev)
 
+    # Offload on against off in the same process: alternating arms of `arm_steps` steps, each
+    # after one untimed step, so slow drift (clocks, host) hits both arms alike. The copy
+    # engines are timed (an event pair per copy) only during the offload-on arms.
+    offload_ab = None
+    if not args.no_offload and args.offload_pairs > 0:
+        arm_steps = max(1, args.offload_arm_steps)
+        arms = {True: [], False: []}
+        d2h_ms = h2d_ms = 0.0
+        d2h_b = h2d_b = moved = 0
+        for _ in range(args.offload_pairs):
+            for enabled in (False, True):
+                model.activation_offload = enabled
+                ring.set_timing(enabled)
+                step(inputs)
+                barrier()
+                if enabled:  # the untimed step's copies are left out of the copy-engine figures
+                    c0, b0 = ring.copy_time(), ring.stats()
+                a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a_ev.record()
+                for _ in range(arm_steps):
+                    step(inputs)
+                b_ev.record()
+                barrier()
+                arms[enabled].append(a_ev.elapsed_time(b_ev) / arm_steps)
+                if enabled:
+                    c1, b1 = ring.copy_time(), ring.stats()
+                    d2h_ms += c1["d2h_ms"] - c0["d2h_ms"]
+                    h2d_ms += c1["h2d_ms"] - c0["h2d_ms"]
+                    d2h_b += c1["d2h_bytes"] - c0["d2h_bytes"]
+                    h2d_b += c1["h2d_bytes"] - c0["h2d_bytes"]
+                    moved += (b1["d2h_bytes"] - b0["d2h_bytes"]) + (b1["h2d_bytes"] - b0["h2d_bytes"])
+        ring.set_timing(False)
+        model.activation_offload = True
+        on_ms, off_ms = statistics.mean(arms[True]), statistics.mean(arms[False])
+        link = host_link_gbs(dev)
+        offload_ab = {
+            "ms_per_step_on": on_ms, "ms_per_step_off": off_ms, "overhead": on_ms / off_ms - 1.0,
+            "arms": {"on": arms[True], "off": arms[False]}, "steps_per_arm": arm_steps,
+            "d2h_copy_engine_gbs": d2h_b / (d2h_ms * 1e-3) / 1e9 if d2h_ms > 0 else None,
+            "h2d_copy_engine_gbs": h2d_b / (h2d_ms * 1e-3) / 1e9 if h2d_ms > 0 else None,
+            "host_link_gbs": link,
+            "d2h_busy_frac_of_step": d2h_ms / (on_ms * arm_steps * args.offload_pairs),
+            "h2d_busy_frac_of_step": h2d_ms / (on_ms * arm_steps * args.offload_pairs),
+            "bytes_per_step": moved / (arm_steps * args.offload_pairs),
+            "note": ("offload on vs off alternated in this run (one untimed step before each arm); copy-engine GB/s = "
+                     "bytes / summed CUDA-event time of the ring's copies; host_link_gbs = best plain 256 MiB "
+                     "pinned->device copy on the idle GPU"),
+        }
+    exchange = None
+    if world > 1:
+        waits = []
+        for _ in range(2):
+            step(inputs)
+            waits.append(reducer.last_wait_ms())
+        exchange = {"buckets": len(reducer.buckets), "bucket_bytes": reducer.bucket_bytes,
+                    "grad_bytes_per_step": sum(reducer.bucket_bytes),
+                    "buckets_sent_during_backward": reducer.last_sent_from_hooks,
+                    "finish_wait_ms": waits,
+                    "note": "finish_wait_ms: device time the compute stream waited in the all-reduce after backward"}
+
     times = torch.tensor([elapsed_ms, e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
@@ -664,6 +834,10 @@ def run_train(args: argparse.Namespace) -> None:
                                   "conditioning, offload gather/scatter"),
             "loss_last": losses[-1] if losses else None,
         }
+        if offload_ab is not None:
+            line["offload"]["ab"] = offload_ab
+        if exchange is not None:
+            line["grad_exchange"] = exchange
         if streamer is not None:
             line["config"]["blocks_to_swap"] = args.blocks_to_swap
             line["block_swap"] = block_swap_summary(swap0, swap1, args.steps, elapsed_ms, dev)

@@ -294,6 +294,13 @@ MOSS_API int moss_offload_host_ptr(void* ring, int64_t ticket, void** host);
 /* Counters: bytes packed, bytes restored, live tickets, reserved pinned bytes. */
 MOSS_API int moss_offload_stats(void* ring, uint64_t* d2h_bytes, uint64_t* h2d_bytes, int64_t* live,
                        uint64_t* pinned_bytes);
+/* Measurement of the copy engines (off by default): with timing on, every later copy gets a
+ * pair of CUDA events on its stream. moss_offload_copy_time waits for the timed copies and
+ * returns their summed durations and bytes, per direction, since timing was first enabled.
+ * New in this library: the reference times nothing (training/activation_offload.py:116-147). */
+MOSS_API int moss_offload_set_timing(void* ring, int enable);
+MOSS_API int moss_offload_copy_time(void* ring, double* d2h_ms, double* h2d_ms, uint64_t* d2h_timed_bytes,
+                           uint64_t* h2d_timed_bytes);
 
 /*
  * Frozen-block stager: the staging-slot state machine of the asynchronous block swap

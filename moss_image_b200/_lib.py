@@ -80,6 +80,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i64),
          ctypes.POINTER(ctypes.c_uint64)],
     ),
+    "moss_offload_set_timing": (_i32, [_vp, _i32]),
+    "moss_offload_copy_time": (
+        _i32,
+        [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint64),
+         ctypes.POINTER(ctypes.c_uint64)],
+    ),
     "moss_block_stager_create": (_i32, [_i32, _i32, _vp, ctypes.POINTER(_vp)]),
     "moss_block_stager_destroy": (_i32, [_vp, _i32]),
     "moss_block_stager_add_block": (_i32, [_vp, _vp, _sz, ctypes.POINTER(_i64)]),

@@ -162,6 +162,19 @@ class OffloadRing:
         )
         return {"d2h_bytes": d2h.value, "h2d_bytes": h2d.value, "live": live.value, "pinned_bytes": pinned.value}
 
+    def set_timing(self, enable: bool) -> None:
+        """Time every later copy with a CUDA event pair on its stream (measurement only)."""
+        _lib.check(_lib.library().moss_offload_set_timing(self.handle, 1 if enable else 0), "moss_offload_set_timing")
+
+    def copy_time(self) -> dict[str, float]:
+        """Summed copy-engine time and bytes of the timed copies, per direction (waits for them)."""
+        d2h_ms, h2d_ms = ctypes.c_double(), ctypes.c_double()
+        d2h_b, h2d_b = ctypes.c_uint64(), ctypes.c_uint64()
+        _lib.check(_lib.library().moss_offload_copy_time(self.handle, ctypes.byref(d2h_ms), ctypes.byref(h2d_ms),
+                                                         ctypes.byref(d2h_b), ctypes.byref(h2d_b)),
+                   "moss_offload_copy_time")
+        return {"d2h_ms": d2h_ms.value, "h2d_ms": h2d_ms.value, "d2h_bytes": d2h_b.value, "h2d_bytes": h2d_b.value}
+
 
 
 

@@ -148,5 +148,26 @@ struct SkinnyPlan {
 SkinnyPlan plan_skinny(int64_t M, int64_t Nc, int64_t Kr, int sms);
 int launch_skinny(bool dx, int v_kind, bool fast, int nt, const Args& a, cudaStream_t stream);
 
+// Split-K epilogue shared by the few-row kernels (w8a16_gemm_skinny.cu):
+// out[m, n] = round_v(sum_s partial[s, m, n] + round_v(bias[n])), splits added in order.
+int launch_splitk_reduce(int v_kind, const float* partial, int splits, int M, int Nc, const void* bias, int bias_kind,
+                         void* out, int out_kind, int64_t ldo, cudaStream_t stream);
+
+// Weight-streaming kernel for at most kStreamMaxRows activation rows without a LoRA term
+// (w8a16_gemm_stream.cu): 16 output features (forward) or 128 output columns (grad-input) per
+// CTA, the reduction split across CTAs when those alone leave SMs idle.
+constexpr int64_t kStreamMaxRows = 16;
+struct StreamPlan {
+  bool usable = false;
+  int splits = 1;     // reduction splits (> 1 needs the workspace for the f32 partials)
+  int per_split = 0;  // slabs per split
+  int ctas = 0;
+  size_t partial_bytes = 0;
+  size_t total() const { return splits > 1 ? partial_bytes : 0; }
+};
+StreamPlan plan_stream(bool dx, int64_t M, int64_t Nc, int64_t Kr, int sms);
+StreamPlan unsplit(StreamPlan p);  // the same plan with the reduction in one CTA per tile
+int launch_stream(bool dx, int v_kind, bool fast, const Args& a, const StreamPlan& p, cudaStream_t stream);
+
 }  // namespace gemm
 }  // namespace moss

@@ -128,8 +128,60 @@ struct OffloadRing {
   cudaEvent_t rewind_fence = nullptr;  // last H2D before a rewind
   bool fence_pending = false;
   uint64_t d2h_bytes = 0, h2d_bytes = 0;
+  // Optional copy-engine timing (moss_offload_set_timing): an event pair around each copy.
+  bool timing = false;
+  struct TimedCopy {
+    cudaEvent_t start = nullptr, end = nullptr;
+    size_t bytes = 0;
+    bool h2d = false;
+  };
+  std::vector<TimedCopy> pending;     // recorded, not yet harvested
+  std::vector<TimedCopy> event_pool;  // harvested pairs, reused
+  double d2h_ms = 0.0, h2d_ms = 0.0;
+  uint64_t d2h_timed_bytes = 0, h2d_timed_bytes = 0;
   std::mutex mu;
 };
+
+// Event pair for one timed copy (from the pool, or new).
+static int timed_copy_begin(OffloadRing& r, bool h2d, size_t bytes, cudaStream_t stream, OffloadRing::TimedCopy* out) {
+  OffloadRing::TimedCopy c;
+  if (!r.event_pool.empty()) {
+    c = r.event_pool.back();
+    r.event_pool.pop_back();
+  } else {
+    MOSS_CUDA_TRY(cudaEventCreate(&c.start));
+    MOSS_CUDA_TRY(cudaEventCreate(&c.end));
+  }
+  c.bytes = bytes;
+  c.h2d = h2d;
+  MOSS_CUDA_TRY(cudaEventRecord(c.start, stream));
+  *out = c;
+  return MOSS_OK;
+}
+
+// Accumulate the copies whose end event has completed (all of them when `wait` is set).
+static void harvest(OffloadRing& r, bool wait) {
+  size_t keep = 0;
+  for (size_t i = 0; i < r.pending.size(); ++i) {
+    OffloadRing::TimedCopy& c = r.pending[i];
+    if (wait) cudaEventSynchronize(c.end);
+    float ms = 0.0f;
+    if (cudaEventQuery(c.end) == cudaSuccess && cudaEventElapsedTime(&ms, c.start, c.end) == cudaSuccess) {
+      if (c.h2d) {
+        r.h2d_ms += ms;
+        r.h2d_timed_bytes += c.bytes;
+      } else {
+        r.d2h_ms += ms;
+        r.d2h_timed_bytes += c.bytes;
+      }
+      r.event_pool.push_back(c);
+    } else {
+      cudaGetLastError();
+      r.pending[keep++] = c;
+    }
+  }
+  r.pending.resize(keep);
+}
 
 static constexpr size_t kAlign = 256;
 
@@ -227,6 +279,14 @@ extern "C" int moss_offload_ring_destroy(void* ring) {
       if (t.d2h_done) cudaEventDestroy(t.d2h_done);
       if (t.h2d_done) cudaEventDestroy(t.h2d_done);
     }
+    for (auto& c : r->pending) {
+      cudaEventDestroy(c.start);
+      cudaEventDestroy(c.end);
+    }
+    for (auto& c : r->event_pool) {
+      cudaEventDestroy(c.start);
+      cudaEventDestroy(c.end);
+    }
     for (Segment& s : r->segments) cudaFreeHost(s.host);
     if (r->rewind_fence) cudaEventDestroy(r->rewind_fence);
   }
@@ -269,8 +329,19 @@ extern "C" int moss_offload_pack(void* ring, const void* src, size_t nbytes, mos
     MOSS_CUDA_TRY(cudaStreamWaitEvent(r.d2h, r.rewind_fence, 0));
     r.fence_pending = false;
   }
-  if (nbytes > 0)
+  if (nbytes > 0) {
+    OffloadRing::TimedCopy tc;
+    if (r.timing) {
+      rc = timed_copy_begin(r, false, nbytes, r.d2h, &tc);
+      if (rc != MOSS_OK) return rc;
+    }
     MOSS_CUDA_TRY(cudaMemcpyAsync(r.segments[seg].host + off, src, nbytes, cudaMemcpyDeviceToHost, r.d2h));
+    if (r.timing) {
+      MOSS_CUDA_TRY(cudaEventRecord(tc.end, r.d2h));
+      r.pending.push_back(tc);
+      if (r.pending.size() > 4096) harvest(r, false);
+    }
+  }
   MOSS_CUDA_TRY(cudaEventRecord(t.d2h_done, r.d2h));
   r.d2h_bytes += nbytes;
   *ticket = id;
@@ -285,8 +356,19 @@ extern "C" int moss_offload_prefetch(void* ring, int64_t ticket, void* dst) {
   if (t == nullptr) return fail(MOSS_ERR_NOT_FOUND, "unknown or released offload ticket %lld", (long long)ticket);
   if (t->bytes > 0 && dst == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null destination");
   MOSS_CUDA_TRY(cudaStreamWaitEvent(r.h2d, t->d2h_done, 0));
-  if (t->bytes > 0)
+  if (t->bytes > 0) {
+    OffloadRing::TimedCopy tc;
+    if (r.timing) {
+      const int rc = timed_copy_begin(r, true, t->bytes, r.h2d, &tc);
+      if (rc != MOSS_OK) return rc;
+    }
     MOSS_CUDA_TRY(cudaMemcpyAsync(dst, r.segments[t->seg].host + t->off, t->bytes, cudaMemcpyHostToDevice, r.h2d));
+    if (r.timing) {
+      MOSS_CUDA_TRY(cudaEventRecord(tc.end, r.h2d));
+      r.pending.push_back(tc);
+      if (r.pending.size() > 4096) harvest(r, false);
+    }
+  }
   MOSS_CUDA_TRY(cudaEventRecord(t->h2d_done, r.h2d));
   t->h2d_issued = true;
   r.h2d_bytes += t->bytes;
@@ -343,5 +425,26 @@ extern "C" int moss_offload_stats(void* ring, uint64_t* d2h_bytes, uint64_t* h2d
   if (h2d_bytes) *h2d_bytes = r.h2d_bytes;
   if (live) *live = r.live;
   if (pinned_bytes) *pinned_bytes = r.reserved;
+  return clear_ok();
+}
+
+extern "C" int moss_offload_set_timing(void* ring, int enable) {
+  if (ring == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null ring");
+  OffloadRing& r = *static_cast<OffloadRing*>(ring);
+  std::lock_guard<std::mutex> lock(r.mu);
+  r.timing = enable != 0;
+  return clear_ok();
+}
+
+extern "C" int moss_offload_copy_time(void* ring, double* d2h_ms, double* h2d_ms, uint64_t* d2h_timed_bytes,
+                                      uint64_t* h2d_timed_bytes) {
+  if (ring == nullptr) return fail(MOSS_ERR_INVALID_ARGUMENT, "null ring");
+  OffloadRing& r = *static_cast<OffloadRing*>(ring);
+  std::lock_guard<std::mutex> lock(r.mu);
+  harvest(r, true);
+  if (d2h_ms) *d2h_ms = r.d2h_ms;
+  if (h2d_ms) *h2d_ms = r.h2d_ms;
+  if (d2h_timed_bytes) *d2h_timed_bytes = r.d2h_timed_bytes;
+  if (h2d_timed_bytes) *h2d_timed_bytes = r.h2d_timed_bytes;
   return clear_ok();
 }

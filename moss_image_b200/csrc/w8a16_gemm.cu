@@ -682,6 +682,21 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
   const int sms = sm_count();
+  if (ext_a == nullptr && M <= kStreamMaxRows) {
+    // A handful of rows: stream the weight at HBM speed, decode in registers, warp-level MMAs.
+    StreamPlan sp = plan_stream(dx, M, Nc, Kr, sms);
+    if (sp.usable) {
+      Args s = a;
+      if (sp.splits > 1 && workspace != nullptr && workspace_bytes >= sp.total() &&
+          (reinterpret_cast<uintptr_t>(workspace) & 255) == 0) {
+        s.partial = static_cast<float*>(workspace);
+      } else {
+        sp = unsplit(sp);
+      }
+      const int rc = launch_stream(dx, v_kind, fast, s, sp, stream);
+      if (rc != MOSS_ERR_UNSUPPORTED) return rc;
+    }
+  }
   if (tma && ext_a == nullptr && !use_pair(M, Nc, sms)) {
     // Too few rows for the CTA-pair tiles: operand-swapped kernel that streams the weight over
     // all SMs (split over K when needed).
@@ -751,6 +766,9 @@ extern "C" int moss_w8a16_gemm_workspace_bytes(int64_t m, int64_t n_out, int64_t
   size_t need = gemm::plan_split(m, n_out, k_red, sms).total();
   const gemm::SkinnyPlan sp = gemm::plan_skinny(m, n_out, k_red, sms);
   if (sp.usable) need = std::max(need, sp.total());
+  // the few-row streaming kernel (either direction: the query does not say which)
+  need = std::max(need, gemm::plan_stream(false, m, n_out, k_red, sms).total());
+  need = std::max(need, gemm::plan_stream(true, m, n_out, k_red, sms).total());
   *bytes = need;
   return clear_ok();
 }

@@ -594,6 +594,19 @@ static int launch_nt(int nt, const CUtensorMap& tx, const CUtensorMap& tw, const
 
 }  // namespace skinny
 
+int launch_splitk_reduce(int v_kind, const float* partial, int splits, int M, int Nc, const void* bias, int bias_kind,
+                         void* out, int out_kind, int64_t ldo, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(M) * ((Nc + 7) / 8);
+  const unsigned grid =
+      static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 8 * skinny::sm_count())));
+  if (v_kind == kBF16)
+    skinny::splitk_reduce_kernel<kBF16><<<grid, 256, 0, stream>>>(partial, splits, M, Nc, bias, bias_kind, out, out_kind, ldo);
+  else
+    skinny::splitk_reduce_kernel<kF16><<<grid, 256, 0, stream>>>(partial, splits, M, Nc, bias, bias_kind, out, out_kind, ldo);
+  MOSS_CUDA_TRY(cudaGetLastError());
+  return MOSS_OK;
+}
+
 SkinnyPlan plan_skinny(int64_t M, int64_t Nc, int64_t Kr, int sms) {
   using namespace skinny;
   SkinnyPlan p;

@@ -145,6 +145,61 @@ def time_block_sample(*, dim: int = 3072, heads: int = 24, mlp_dim: int = 12288,
     return {"seconds": times, "threads": torch.get_num_threads(), "seq": seq}
 
 
+def time_config1_ops(*, m: int = 4096, k: int = 3072, n: int = 3072, reps: int = 5, warmup: int = 2,
+                     threads: int | None = None) -> dict:
+    """The reference's CPU path for the benchmark's single-linear configuration, op by op.
+
+    X bf16 [m, k] ~ N(0, 1), W [n, k] ~ N(0, 0.02) quantised per output channel (the oracle
+    quantiser, training/quantization.py:87-91), bias bf16 zeros, dY bf16 [m, n] ~ N(0, 1):
+    * forward: the eager ``F.linear(x, dec(W), bias)`` (training/quantization.py:43);
+    * grad-input: ``dY @ dec(W)`` (training/quantization.py:61-64);
+    * offload round trip of X: on CPU the reference's hooks are a no-op
+      (training/activation_offload.py:92-93), so the pack/unpack pair is restated as the two
+      host copies it would make: the dense payload into a new buffer (pack,
+      training/activation_offload.py:123-126) and back into an ``empty_strided`` tensor
+      (unpack, :139-147).
+    Median seconds of ``reps`` after ``warmup`` untimed repetitions, on ``threads`` threads.
+    """
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = np.random.default_rng(0)
+    w = gen.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+    q, s, _ = O.quantize(w)
+    qt, st = torch.from_numpy(q), torch.from_numpy(s)
+    tg = torch.Generator().manual_seed(0)
+    x = torch.randn(m, k, generator=tg).to(torch.bfloat16)
+    dy = torch.randn(m, n, generator=tg).to(torch.bfloat16)
+    bias = torch.zeros(n, dtype=torch.bfloat16)
+
+    def fwd() -> None:
+        F.linear(x, _dequantize(qt, st, torch.bfloat16), bias)
+
+    def dx() -> None:
+        dy.matmul(_dequantize(qt, st, torch.bfloat16))
+
+    def round_trip() -> None:
+        packed = torch.empty(x.shape, dtype=x.dtype)
+        packed.copy_(x)
+        restored = torch.empty_strided(x.shape, x.stride(), dtype=x.dtype)
+        restored.copy_(packed)
+
+    out = {"threads": torch.get_num_threads(), "shape": [m, k, n], "reps": reps, "warmup": warmup}
+    for name, fn in (("fwd", fwd), ("dx", dx), ("offload_round_trip", round_trip)):
+        for _ in range(warmup):
+            fn()
+        times = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        out[f"{name}_s"] = float(np.median(times))
+    flops = 2.0 * m * n * k
+    out["fwd_tflops"] = flops / out["fwd_s"] / 1e12
+    out["dx_tflops"] = flops / out["dx_s"] / 1e12
+    out["offload_round_trip_gbs"] = 2.0 * x.numel() * x.element_size() / out["offload_round_trip_s"] / 1e9
+    return out
+
+
 def cpu_model_name() -> str:
     try:
         with open("/proc/cpuinfo") as fh:
