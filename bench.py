@@ -61,7 +61,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--offload-pairs", type=int, default=2,
                    help="alternated (offload off, offload on) arm pairs timed after the main region (0: none)")
     p.add_argument("--offload-arm-steps", type=int, default=3)
-    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx", "comfy_load",
+    p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx",
+                                        "convrot_dx_separate", "comfy_load",
                                         "segment_modulate", "segment_gate", "rmsnorm", "rmsnorm_bwd"], default=None)
     p.add_argument("--group", type=int, default=256, help="ConvRot / Hadamard group size")
     p.add_argument("--m", type=int, default=9216)
@@ -369,10 +370,15 @@ def run_kernel(args: argparse.Namespace) -> None:
     elif args.kernel == "convrot_fwd":
         x = torch.randn(m, k, device=dev, generator=gen).to(torch.bfloat16)
         fn = lambda: qk.convrot_forward(x, q, s, None, torch.bfloat16, torch.bfloat16, args.group)  # noqa: E731
-    elif args.kernel == "convrot_dx":
+    elif args.kernel in ("convrot_dx", "convrot_dx_separate"):
         dy = torch.randn(m, n, device=dev, generator=gen).to(torch.bfloat16)
-        fn = lambda: qk.convrot_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16,  # noqa: E731
-                                         args.group)
+        if args.kernel == "convrot_dx":  # rotation in the grad-input GEMM's epilogue where it applies
+            fn = lambda: qk.convrot_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16,  # noqa: E731
+                                             torch.bfloat16, args.group)
+        else:  # the GEMM, then the rotation kernel over its output
+            def fn():
+                dx = qk.int8_linear_backward(dy, q, s, torch.Size((m, k)), torch.bfloat16, torch.bfloat16)
+                return qk.hadamard_transform(dx, args.group, out=dx)
     elif args.kernel in ("rmsnorm", "rmsnorm_bwd"):
         from moss_image_b200.norms import rms_norm
 

@@ -198,6 +198,20 @@ MOSS_API int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64_t
                        moss_stream_t stream);
 
 /*
+ * ConvRot grad-input: dx = H * (dy * dec(q)), i.e. moss_w8a16_gemm_dx (no LoRA term) followed
+ * by the grouped Hadamard rotation of moss_hadamard_rotate on each row of dx, with the same
+ * roundings (the GEMM output rounded to dx_dtype, then every radix stage). When the CTA-pair
+ * kernel runs the GEMM and group is 256, the rotation is applied to the accumulator rows in its
+ * epilogue (no second pass over dx); otherwise the rotation kernel runs on dx afterwards, on the
+ * same stream. group: a power of two <= 8192 that divides k. Replaces triton_convrot_backward
+ * (training/quant_kernels.py:469-504), which runs the GEMM and then one kernel per radix stage.
+ */
+MOSS_API int moss_w8a16_gemm_dx_rotated(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
+                               const float* scale, int weight_dtype, int64_t k, int64_t group, void* dx,
+                               int dx_dtype, void* workspace, size_t workspace_bytes, int* status,
+                               moss_stream_t stream);
+
+/*
  * Grouped normalised Hadamard rotation of the last dimension (ConvRot), y = x . H with H
  * block-diagonal in `group`-sized blocks (a power of two, at most 8192) built from the
  * regular H4 and one H2 factor for odd log2(group). H is symmetric and orthonormal, so the

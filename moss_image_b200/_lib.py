@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _vp, _i32, _i64, _f32, _vp, _i32, _vp, _sz, _vp, _vp],
     ),
+    "moss_w8a16_gemm_dx_rotated": (
+        _i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp, _sz, _vp, _vp]),
     "moss_hadamard_rotate": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp]),
     "moss_segment_modulate": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i32, _i64, _vp, _i64, _vp, _vp]),
     "moss_segment_modulate_bwd": (

@@ -37,6 +37,9 @@ struct Args {
   // tail_splits units each, whose f32 partials go to `partial` [tail tile][split][256][256]
   // and are summed by a reduction kernel after the GEMM. tail_first = tiles: no split.
   int tail_first, tail_splits;
+  // ConvRot grad-input (CTA-pair kernel only): rotate each output row by the grouped Hadamard
+  // transform of this group size in the epilogue; 0 = no rotation.
+  int rot_group;
 };
 
 // k-block schedule of one work unit: iteration i -> weight k-block or LoRA block.

@@ -597,10 +597,14 @@ static SplitPlan plan_split(int64_t M, int64_t Nc, int64_t Kr, int sms) {
 
 // Shared driver for both directions.
 //   A: [M, Kr] in v_kind (x or dy); weight q: [w_rows, w_cols]; C: [M, Nc]
+//   rot_group > 1 (grad-input only): ask the CTA-pair kernel to apply the ConvRot rotation in its
+//   epilogue; *rotated reports whether it did (otherwise the caller rotates the output).
 static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, int64_t Nc, const int8_t* q,
                const float* scale, int w_kind, int64_t w_rows, int64_t w_cols, const void* bias, int bias_kind,
                const void* ext_a, const void* ext_b, int ext_b_kind, int64_t ext_r, float ext_scale, void* out,
-               int out_kind, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream) {
+               int out_kind, void* workspace, size_t workspace_bytes, int* status, cudaStream_t stream,
+               int64_t rot_group = 0, bool* rotated = nullptr) {
+  if (rotated != nullptr) *rotated = false;
   if (M < 0 || Kr < 0 || Nc < 0) return fail(MOSS_ERR_INVALID_ARGUMENT, "negative GEMM shape");
   if (v_kind != kBF16 && v_kind != kF16)
     return fail(MOSS_ERR_UNSUPPORTED, "compute dtype must be float16 or bfloat16 (got code %d)", v_kind);
@@ -662,6 +666,7 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.counters = nullptr;
   a.tail_first = a.tiles_m * a.tiles_n;  // the CTA-pair kernel's last-round split: none
   a.tail_splits = 1;
+  a.rot_group = 0;
 
   CUtensorMap ta, tw, te;
   memset(&ta, 0, sizeof(ta));
@@ -682,6 +687,20 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.manual = tma ? 0 : 1;
   const bool fast = (w_kind == v_kind);
   const int sms = sm_count();
+  if (dx && rot_group > 1 && tma && ext_a == nullptr && use_pair(M, Nc, sms)) {
+    // ConvRot grad-input with the rotation in the CTA-pair epilogue (whole tiles, no split)
+    Args a2 = a;
+    a2.tiles_m = static_cast<int>((M + 255) / 256);
+    a2.tiles_n = static_cast<int>((Nc + 255) / 256);
+    a2.tail_first = a2.tiles_m * a2.tiles_n;
+    a2.tail_splits = 1;
+    a2.rot_group = static_cast<int>(rot_group);
+    const int rc = launch_pair(dx, v_kind, fast, a2, stream);
+    if (rc != MOSS_ERR_UNSUPPORTED) {
+      if (rc == MOSS_OK && rotated != nullptr) *rotated = true;
+      return rc;
+    }
+  }
   if (ext_a == nullptr && M <= kStreamMaxRows) {
     // A handful of rows: stream the weight at HBM speed, decode in registers, warp-level MMAs.
     StreamPlan sp = plan_stream(dx, M, Nc, Kr, sms);
@@ -792,6 +811,22 @@ extern "C" int moss_w8a16_gemm_dx(const void* dy, int dy_dtype, int64_t m, int64
   const int rc = gemm::run(true, dy, dy_dtype, m, n, k, q, scale, weight_dtype, n, k, nullptr, 0, lora_dyb, lora_a,
                            lora_a_dtype, lora_rank, lora_scale, dx, dx_dtype, workspace, workspace_bytes, status,
                            reinterpret_cast<cudaStream_t>(stream));
+  return rc == MOSS_OK ? clear_ok() : rc;
+}
+
+extern "C" int moss_w8a16_gemm_dx_rotated(const void* dy, int dy_dtype, int64_t m, int64_t n, const int8_t* q,
+                                          const float* scale, int weight_dtype, int64_t k, int64_t group, void* dx,
+                                          int dx_dtype, void* workspace, size_t workspace_bytes, int* status,
+                                          moss_stream_t stream) {
+  if (group < 1 || (group & (group - 1)) != 0 || group > 8192 || (k > 0 && k % group != 0))
+    return fail(MOSS_ERR_INVALID_ARGUMENT, "rotation group %lld must be a power of two <= 8192 dividing k=%lld",
+                static_cast<long long>(group), static_cast<long long>(k));
+  bool rotated = false;
+  int rc = gemm::run(true, dy, dy_dtype, m, n, k, q, scale, weight_dtype, n, k, nullptr, 0, nullptr, nullptr, 0, 0, 1.0f,
+                     dx, dx_dtype, workspace, workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream), group,
+                     &rotated);
+  if (rc != MOSS_OK) return rc;
+  if (!rotated && group > 1 && m > 0 && k > 0) rc = moss_hadamard_rotate(dx, dx_dtype, m, k, group, dx, stream);
   return rc == MOSS_OK ? clear_ok() : rc;
 }
 

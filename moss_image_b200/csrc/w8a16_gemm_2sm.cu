@@ -219,6 +219,116 @@ __global__ void __launch_bounds__(256) pair_tail_reduce_kernel(const Args args) 
   }
 }
 
+// ConvRot grad-input epilogue: the grouped Hadamard rotation (group 256 = one tile width) of
+// one output row, with the arithmetic and the per-stage rounding of the standalone rotation
+// kernel for 16-bit data (hadamard.cu, reference training/quant_kernels.py:231-277), so
+// GEMM-then-rotate and the fused epilogue agree bit for bit: the row is first rounded to the
+// compute kind (the GEMM output), every radix-4 stage (total * 0.5 - x, in f32) is rounded to it
+// again. The fused path is used only when the output kind is the compute kind.
+constexpr int kRotGroup = 256;
+template <int kV>
+__device__ __forceinline__ void rot_round_pair(float& a, float& b) {
+  const uint32_t p = pack2_kind<kV>(a, b);
+  if constexpr (kV == kBF16) {
+    a = __uint_as_float(p << 16);
+    b = __uint_as_float(p & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&p));
+    a = f.x;
+    b = f.y;
+  }
+}
+__device__ __forceinline__ void rot_radix4(float& a, float& b, float& c, float& d) {
+  const float half = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d), 0.5f);
+  const float na = __fsub_rn(half, d), nb = __fsub_rn(half, c), nc = __fsub_rn(half, b), nd = __fsub_rn(half, a);
+  a = na;
+  b = nb;
+  c = nc;
+  d = nd;
+}
+template <int kV, int N>
+__device__ __forceinline__ void rot_round_all(float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i += 2) rot_round_pair<kV>(v[i], v[i + 1]);
+}
+
+// Rotates the 256 accumulator columns of this thread's TMEM row in place (radix-4 stages of
+// stride 1, 4 and 16 inside each 64-column window, through registers), then applies the
+// stride-64 stage on four 16-column slices at a time and stores the rounded outputs.
+template <int kV>
+__device__ __forceinline__ void rotate_store_row(const Args& args, uint32_t tacc, int row, int col0, bool row_ok,
+                                                 bool vec_ok) {
+#pragma unroll 1
+  for (int w = 0; w < 4; ++w) {
+    uint32_t r[64];
+    tmem_ld_32x32b_x32(tacc + w * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    tmem_ld_32x32b_x32(tacc + w * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    tmem_wait_ld();
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+    rot_round_all<kV>(v);
+#pragma unroll
+    for (int b = 0; b < 16; ++b) rot_radix4(v[4 * b], v[4 * b + 1], v[4 * b + 2], v[4 * b + 3]);
+    rot_round_all<kV>(v);
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int p = 0; p < 4; ++p) rot_radix4(v[16 * b + p], v[16 * b + p + 4], v[16 * b + p + 8], v[16 * b + p + 12]);
+    rot_round_all<kV>(v);
+#pragma unroll
+    for (int p = 0; p < 16; ++p) rot_radix4(v[p], v[p + 16], v[p + 32], v[p + 48]);
+    rot_round_all<kV>(v);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(v[16 * h + i]);
+      tmem_st_32x32b_x16(tacc + w * 64 + 16 * h, o);
+    }
+    tmem_wait_st();
+  }
+#pragma unroll 1
+  for (int j0 = 0; j0 < 64; j0 += 16) {
+    uint32_t r[4][16];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x16(tacc + c * 64 + j0, r[c]);
+    tmem_wait_ld();
+    uint32_t p[4][8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      float v0[2], v1[2], v2[2], v3[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        v0[e] = __uint_as_float(r[0][i + e]);
+        v1[e] = __uint_as_float(r[1][i + e]);
+        v2[e] = __uint_as_float(r[2][i + e]);
+        v3[e] = __uint_as_float(r[3][i + e]);
+        rot_radix4(v0[e], v1[e], v2[e], v3[e]);
+      }
+      p[0][i / 2] = pack2_kind<kV>(v0[0], v0[1]);
+      p[1][i / 2] = pack2_kind<kV>(v1[0], v1[1]);
+      p[2][i / 2] = pack2_kind<kV>(v2[0], v2[1]);
+      p[3][i / 2] = pack2_kind<kV>(v3[0], v3[1]);
+    }
+    if (!row_ok) continue;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int64_t off = static_cast<int64_t>(row) * args.ldo + col0 + c * 64 + j0;
+      uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
+      if (vec_ok) {
+        stg256(dst, p[c]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          dst[2 * e] = static_cast<uint16_t>(p[c][e] & 0xFFFFu);
+          dst[2 * e + 1] = static_cast<uint16_t>(p[c][e] >> 16);
+        }
+      }
+    }
+  }
+}
+
 struct Barriers {
   uint64_t a_full[kAStages];   // local: this CTA's A half landed
   uint64_t a_empty[kAStages];  // local: A stage free (MMA commit)
@@ -235,7 +345,7 @@ struct Barriers {
 };
 static_assert(sizeof(Barriers) <= 512, "barrier block too large");
 
-template <bool kDX, int kV, bool kFast>
+template <bool kDX, int kV, bool kFast, bool kRot>
 __global__ void __launch_bounds__(kThreads, 1)
     w8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_ext, const Args args) {
@@ -464,6 +574,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < args.M;
       const bool vec_ok = (args.out_kind != kF32) && ((args.ldo & 15) == 0) &&
                           ((reinterpret_cast<uintptr_t>(args.out) & 31) == 0);
+      if constexpr (kRot) {
+        // whole tiles only (the host disables the last-round split and needs Nc % 256 == 0)
+        rotate_store_row<kV>(args, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kTileN),
+                             row, n0, row_ok, vec_ok);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t eb = bar(bars->acc_empty[acc]);
+          if (leader)
+            mbar_arrive(eb);
+          else
+            mbar_arrive_cluster(mapa_shared(eb, 0));
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < kTileN / 32; ++c) {
         uint32_t r[32];
@@ -683,10 +808,10 @@ static int sm_count() {
   return n;
 }
 
-template <bool kDX, int kV, bool kFast>
+template <bool kDX, int kV, bool kFast, bool kRot = false>
 static int launch_typed(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& te, const Args& a,
                         cudaStream_t stream) {
-  auto kern = w8_gemm_pair_kernel<kDX, kV, kFast>;
+  auto kern = w8_gemm_pair_kernel<kDX, kV, kFast, kRot>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   static int max_pairs = 0;
@@ -792,6 +917,17 @@ int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t s) {
   if (a.ext_r > 0 && !make_map(&te, v_dt, 2, a.ext_a, a.ext_r, a.M, a.ld_ext_a * 2, BK, kHalf,
                                CU_TENSOR_MAP_SWIZZLE_128B))
     return MOSS_ERR_UNSUPPORTED;
+  if (a.rot_group != 0) {
+    // ConvRot grad-input rotated in the epilogue: whole 256-column tiles, no last-round split
+    if (!dx || a.rot_group != kRotGroup || a.Nc % kTileN != 0 || a.tail_splits != 1 || a.ext_r > 0 ||
+        a.out_kind != v_kind)
+      return MOSS_ERR_UNSUPPORTED;
+    if (v_kind == kBF16)
+      return fast ? launch_typed<true, kBF16, true, true>(ta, tw, te, a, s)
+                  : launch_typed<true, kBF16, false, true>(ta, tw, te, a, s);
+    return fast ? launch_typed<true, kF16, true, true>(ta, tw, te, a, s)
+                : launch_typed<true, kF16, false, true>(ta, tw, te, a, s);
+  }
   if (dx) {
     if (v_kind == kBF16)
       return fast ? launch_typed<true, kBF16, true>(ta, tw, te, a, s) : launch_typed<true, kBF16, false>(ta, tw, te, a, s);

@@ -318,12 +318,16 @@ def int8_linear_backward(
     lora_dyb: torch.Tensor | None = None,
     lora_a: torch.Tensor | None = None,
     lora_scale: float = 1.0,
+    rotate_group: int = 1,
 ) -> torch.Tensor:
     """dX = dY dec(W) (+ lora_scale * lora_dyb lora_a) on the sm_100a kernel.
 
     Reference: ``triton_int8_linear_backward``, training/quant_kernels.py:337-373. The
     product is rounded to the gradient's compute dtype and stored as ``input_dtype``.
     The int8 weight is consumed in its ``[N, K]`` storage order (no transpose copy).
+    With ``rotate_group`` > 1 (ConvRot, no LoRA term) each row of dX is then rotated by the
+    grouped Hadamard transform (``moss_w8a16_gemm_dx_rotated``: in the GEMM's epilogue when the
+    CTA-pair kernel runs, else by the rotation kernel right after it).
     """
     compute_dtype = gradient.dtype if compute_dtype is None else compute_dtype
     v_kind = _compute_kind(compute_dtype)
@@ -359,18 +363,30 @@ def int8_linear_backward(
     status = status_buffer(gradient.device)
     ws_owner, ws, ws_bytes = _workspace(rows, in_features, out_features, gradient.device)
     done = _launch_observer("dx", rows, in_features, out_features, gradient.device) if _launch_observer else None
-    rc = lib.moss_w8a16_gemm_dx(
-        _lib.ptr(matrix), v_kind, rows, out_features,
-        _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features,
-        _lib.ptr(lora_dyb), _lib.ptr(lora_a), _lib.DTYPE_CODES.get(lora_a.dtype, -1) if lora_a is not None else 0,
-        rank, float(lora_scale),
-        _lib.ptr(grad_input), _lib.dtype_code(input_dtype), ws, ws_bytes,
-        _lib.ptr(status), _lib.stream_handle(gradient.device),
-    )
+    if rotate_group > 1:
+        if lora_dyb is not None:
+            raise ValueError("a rotated grad-input takes no LoRA term")
+        rc = lib.moss_w8a16_gemm_dx_rotated(
+            _lib.ptr(matrix), v_kind, rows, out_features,
+            _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features, int(rotate_group),
+            _lib.ptr(grad_input), _lib.dtype_code(input_dtype), ws, ws_bytes,
+            _lib.ptr(status), _lib.stream_handle(gradient.device),
+        )
+        what = "moss_w8a16_gemm_dx_rotated"
+    else:
+        rc = lib.moss_w8a16_gemm_dx(
+            _lib.ptr(matrix), v_kind, rows, out_features,
+            _lib.ptr(weight), _lib.ptr(scale), _lib.dtype_code(weight_dtype), in_features,
+            _lib.ptr(lora_dyb), _lib.ptr(lora_a), _lib.DTYPE_CODES.get(lora_a.dtype, -1) if lora_a is not None else 0,
+            rank, float(lora_scale),
+            _lib.ptr(grad_input), _lib.dtype_code(input_dtype), ws, ws_bytes,
+            _lib.ptr(status), _lib.stream_handle(gradient.device),
+        )
+        what = "moss_w8a16_gemm_dx"
     if done is not None:
         done()
     del ws_owner
-    _lib.check(rc, "moss_w8a16_gemm_dx")
+    _lib.check(rc, what)
     return grad_input.reshape(input_shape)
 
 
@@ -511,18 +527,18 @@ def convrot_backward(
     weight_dtype: torch.dtype,
     group_size: int,
 ) -> torch.Tensor:
-    """ConvRot input gradient ``H (dY dec(W H))``: the int8 grad-input GEMM, then the rotation
-    in place on its output (H is symmetric and orthonormal).
+    """ConvRot input gradient ``H (dY dec(W H))`` (H is symmetric and orthonormal): one call of
+    ``moss_w8a16_gemm_dx_rotated``, which rotates the GEMM's output rows in the CTA-pair
+    epilogue (group 256) or runs the rotation kernel on them right after the GEMM.
 
-    Reference: ``triton_convrot_backward``, training/quant_kernels.py:469-504.
+    Reference: ``triton_convrot_backward``, training/quant_kernels.py:469-504 (same roundings:
+    the GEMM output in the input dtype, then every radix stage).
     """
     matrix = _matrix_view(gradient.contiguous())
     rows = matrix.shape[0]
     in_features = weight.shape[1]
     grad_input = int8_linear_backward(matrix, weight, scale, torch.Size((rows, in_features)), input_dtype,
-                                      weight_dtype)
-    if rows:
-        hadamard_transform(grad_input, group_size, out=grad_input)
+                                      weight_dtype, rotate_group=group_size)
     return grad_input.reshape(input_shape)
 
 

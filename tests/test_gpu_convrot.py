@@ -8,6 +8,7 @@ of the oracle, and within the reference's own eager-vs-GPU tolerance of its eage
 
 from __future__ import annotations
 
+import ctypes
 import io
 
 import numpy as np
@@ -16,6 +17,7 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from moss_image_b200 import _lib
 from moss_image_b200 import quant_kernels as qk
 from moss_image_b200.convrot import FrozenConvRotLinear, quantize_frozen_convrot_linears
 from oracle import oracle as O
@@ -161,3 +163,87 @@ def test_lora_over_a_convrot_base_adds_the_update_to_the_rotated_product(cuda_de
                     + lora.scale * (x.float() @ lora.lora_A.float().t()) @ lora.lora_B.float().t())
     assert O.rel_fro(_np(y), expected.cpu().numpy()) <= 1e-2
     assert lora.lora_A.grad is not None and torch.isfinite(lora.lora_A.grad).all()
+
+
+def _dx_then_rotate(dy, q, s, k, group, out_dtype, device):
+    """moss_w8a16_gemm_dx without a workspace (no last-round split) then moss_hadamard_rotate."""
+    m, n = dy.shape
+    out = torch.empty(m, k, dtype=out_dtype, device=device)
+    status = qk.status_buffer(device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    lib = _lib.library()
+    codes = {torch.bfloat16: 1, torch.float16: 0, torch.float32: 2}
+    v = codes[dy.dtype]
+    _lib.check(lib.moss_w8a16_gemm_dx(dy.data_ptr(), v, m, n, q.data_ptr(), s.data_ptr(), v, k, None, None, 0, 0, 1.0,
+                                      out.data_ptr(), codes[out_dtype], None, 0, status.data_ptr(), stream), "dx")
+    _lib.check(lib.moss_hadamard_rotate(out.data_ptr(), codes[out_dtype], m, k, group, out.data_ptr(), stream), "rot")
+    return out
+
+
+def _dx_rotated(dy, q, s, k, group, out_dtype, device, *, workspace=True):
+    m, n = dy.shape
+    out = torch.full((m, k), float("nan"), dtype=out_dtype, device=device)
+    codes = {torch.bfloat16: 1, torch.float16: 0, torch.float32: 2}
+    v = codes[dy.dtype]
+    size = ctypes.c_size_t()
+    lib = _lib.library()
+    _lib.check(lib.moss_w8a16_gemm_workspace_bytes(m, k, n, ctypes.byref(size)), "ws")
+    owner = torch.empty(size.value + 256, dtype=torch.uint8, device=device)
+    ws = (owner.data_ptr() + 255) // 256 * 256 if workspace else None
+    _lib.check(lib.moss_w8a16_gemm_dx_rotated(dy.data_ptr(), v, m, n, q.data_ptr(), s.data_ptr(), v, k, group,
+                                              out.data_ptr(), codes[out_dtype], ws, size.value if workspace else 0,
+                                              qk.status_buffer(device).data_ptr(),
+                                              torch.cuda.current_stream(device).cuda_stream), "dx_rotated")
+    torch.cuda.synchronize(device)
+    del owner
+    return out
+
+
+@pytest.mark.parametrize("m,k,n,dtype,out_dtype", [
+    (2048, 3072, 3072, torch.bfloat16, torch.bfloat16),   # CTA-pair kernel: rotation in the epilogue
+    (2100, 3072, 1536, torch.bfloat16, torch.bfloat16),   # ragged last row tile
+    (9216, 3072, 3072, torch.bfloat16, torch.bfloat16),   # the benchmark step's q/k/v/o grad-input shape
+    (4608, 12288, 3072, torch.bfloat16, torch.bfloat16),  # MLP down-projection input gradient, K = 12288
+    (2048, 3072, 3072, torch.float16, torch.float16),
+    (2048, 3072, 3072, torch.bfloat16, torch.float32),    # fp32 input under bf16 compute: stages unrounded
+    (64, 3072, 3072, torch.bfloat16, torch.bfloat16),     # few rows: GEMM, then the rotation kernel
+])
+def test_rotated_grad_input_equals_gemm_then_rotation_bit_for_bit(cuda_device, m, k, n, dtype, out_dtype):
+    """H (dY dec(W H)) fused into the CTA-pair epilogue (group 256) equals the grad-input GEMM
+    followed by the standalone rotation kernel (itself bit-exact with the oracle's staged
+    transform, training/quant_kernels.py:231-277) exactly, and is within the GEMM bar of the
+    oracle."""
+    gen = torch.Generator(device=cuda_device).manual_seed(m + k + n)
+    q = torch.randint(-127, 128, (n, k), generator=gen, device=cuda_device, dtype=torch.int8)
+    s = torch.rand(n, generator=gen, device=cuda_device) * 4e-4 + 1e-4
+    dy = torch.randn(m, n, generator=gen, device=cuda_device).to(dtype)
+    expected = _dx_then_rotate(dy, q, s, k, 256, out_dtype, cuda_device)
+    fused = m >= 2048 and out_dtype == dtype  # the CTA-pair epilogue rotates (never a split plan)
+    for workspace in (True, False):
+        got = _dx_rotated(dy, q, s, k, 256, out_dtype, cuda_device, workspace=workspace)
+        if fused or not workspace:
+            assert torch.equal(got.view(torch.int16 if out_dtype != torch.float32 else torch.int32),
+                               expected.view(torch.int16 if out_dtype != torch.float32 else torch.int32))
+        else:  # a split plan groups the f32 sums differently: last-bit differences of the GEMM output
+            assert O.rel_fro(_np(got), _np(expected)) <= REL_FRO_TOL / 2
+    assert qk.check_device_status(cuda_device) & _lib.STATUS_TIMEOUT_MASK == 0
+    rows = torch.arange(0, m, max(1, m // 48), device=cuda_device)
+    dec = (q.to(torch.bfloat16) * s.to(torch.bfloat16)[:, None]).float().cpu().numpy()
+    ref = (dy[rows].float().cpu().numpy().astype(np.float64) @ dec.astype(np.float64))
+    ref_rot = O.hadamard(ref.astype(np.float32), 256, O.F32)
+    assert O.rel_fro(_np(got[rows]), ref_rot) <= REL_FRO_TOL
+
+
+def test_convrot_module_backward_uses_the_rotated_grad_input(cuda_device):
+    """The module's input gradient at a CTA-pair shape equals rotate(GEMM) bit for bit."""
+    m, k, n = 2048, 3072, 1024
+    gen = torch.Generator().manual_seed(31)
+    base = nn.Linear(k, n, bias=False).requires_grad_(False)
+    with torch.no_grad():
+        base.weight.normal_(0.0, 0.02, generator=gen)
+    module = FrozenConvRotLinear(base.to(cuda_device)).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=gen).to(cuda_device, torch.bfloat16).requires_grad_(True)
+    g = torch.randn(m, n, generator=gen).to(cuda_device, torch.bfloat16)
+    module(x).backward(g)
+    expected = _dx_then_rotate(g, module.weight_int8, module.weight_scale, k, 256, torch.bfloat16, cuda_device)
+    assert torch.equal(x.grad.view(torch.int16), expected.view(torch.int16))
