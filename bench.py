@@ -55,6 +55,8 @@ def parse_args() -> argparse.Namespace:
                    help="stream the frozen int8 weights of the last N blocks from pinned host memory (async)")
     p.add_argument("--packed", default=None,
                    help="heterogeneous batch 'img:txt,img:txt,...': time one packed traversal against per-sample ones")
+    p.add_argument("--full-qkvo", action="store_true",
+                   help="train the q/k/v/o projections in full (bf16 masters) instead of LoRA; other linears int8")
     p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
     p.add_argument("--txt-tokens", type=int, default=TXT_TOKENS)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -639,7 +641,8 @@ def run_train(args: argparse.Namespace) -> None:
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
-    model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0)
+    model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0,
+                             full_qkvo=args.full_qkvo)
     model.train()
     streamer = None
     if args.blocks_to_swap:
@@ -817,9 +820,12 @@ def run_train(args: argparse.Namespace) -> None:
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": (f"{args.depth}-block synthetic DiT int8-W LoRA training step per GPU (batch "
+            "config": {"workload": (f"{args.depth}-block synthetic DiT int8-W {'full-q/k/v/o' if args.full_qkvo else 'LoRA'} "
+                                    f"training step per GPU (batch "
                                     f"{args.batch} x ({img_tokens} img + {txt_tokens} txt) tokens, width {DIM}, MLP {MLP} "
-                                    f"GELU, per-block adaLN {DIM}->{6 * DIM}, LoRA r{RANK} q/k/v/o, grad checkpointing, "
+                                    f"GELU, per-block adaLN {DIM}->{6 * DIM}, "
+                                    + ("q/k/v/o trained in full (bf16 masters), " if args.full_qkvo
+                                       else f"LoRA r{RANK} q/k/v/o, ") + "grad checkpointing, "
                                     f"activation offload {'on' if model.activation_offload else 'off'}"
                                     + (f", int8 blocks streamed from pinned host: last {args.blocks_to_swap}"
                                        if args.blocks_to_swap else "") + ")"),

@@ -240,12 +240,17 @@ def _inject_block(layer: SyntheticBlock, rank: int, alpha: float, targets: tuple
 
 def build_lora_model(depth: int, *, device: torch.device, dim: int = 3072, heads: int = 24, mlp_dim: int = 12288,
                      rank: int = 32, alpha: float | None = None, seed: int = 0,
-                     dtype: torch.dtype = torch.bfloat16) -> SyntheticDiT:
+                     dtype: torch.dtype = torch.bfloat16, full_qkvo: bool = False) -> SyntheticDiT:
     """Random-init stack (weights ~ N(0, 0.02)), int8 base, LoRA on q/k/v/o.
 
     Mirrors the trainer's order (training/train.py:577-589): build, cast, inject LoRA,
     quantise the frozen linears - done block by block on the device so that the
     full-precision weights of only one block exist at a time.
+
+    With ``full_qkvo`` the q/k/v/o projections are trained in full instead (trainable
+    ``dtype`` masters, no adapters) and every other linear is frozen int8: the hybrid that
+    ``quantize_frozen_linears`` allows at module level (training/quantization.py:156-157;
+    the reference trainer itself only pairs int8 bases with LoRA, training/train.py:543-545).
     """
     torch.manual_seed(seed)
     alpha = float(rank if alpha is None else alpha)
@@ -265,7 +270,11 @@ def build_lora_model(depth: int, *, device: torch.device, dim: int = 3072, heads
                         module.bias.zero_()
         block.to(dtype=dtype)
         block.requires_grad_(False)
-        _inject_block(block, rank, alpha, ("q", "k", "v", "o"), 0.01)
+        if full_qkvo:
+            for name in ("q", "k", "v", "o"):
+                block.proj[name].requires_grad_(True)
+        else:
+            _inject_block(block, rank, alpha, ("q", "k", "v", "o"), 0.01)
         quantize_frozen_linears(block)
         layers.append(block)
     model.layers = nn.ModuleList(layers)
