@@ -55,6 +55,8 @@ def parse_args() -> argparse.Namespace:
                    help="stream the frozen int8 weights of the last N blocks from pinned host memory (async)")
     p.add_argument("--packed", default=None,
                    help="heterogeneous batch 'img:txt,img:txt,...': time one packed traversal against per-sample ones")
+    p.add_argument("--no-numa-bind", action="store_true",
+                   help="do not restrict each rank to the CPU cores local to its GPU")
     p.add_argument("--full-qkvo", action="store_true",
                    help="train the q/k/v/o projections in full (bf16 masters) instead of LoRA; other linears int8")
     p.add_argument("--img-tokens", type=int, default=IMG_TOKENS)
@@ -63,6 +65,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--offload-pairs", type=int, default=2,
                    help="alternated (offload off, offload on) arm pairs timed after the main region (0: none)")
     p.add_argument("--offload-arm-steps", type=int, default=3)
+    p.add_argument("--offload-defer-mb", type=int, default=640,
+                   help="keep up to this many MiB of the newest saved activations on the GPU (copied out only when "
+                        "newer ones push them past the budget)")
     p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx",
                                         "convrot_dx_separate", "comfy_load",
                                         "segment_modulate", "segment_gate", "rmsnorm", "rmsnorm_bwd"], default=None)
@@ -573,6 +578,7 @@ def run_packed(args: argparse.Namespace) -> None:
     model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0)
     model.train()
     model.activation_offload = not args.no_offload
+    model.activation_offload_defer_bytes = args.offload_defer_mb << 20
     opt = torch.optim.AdamW([p for p in model.parameters() if p.requires_grad], lr=1e-4, fused=True)
     gen = torch.Generator(device=dev).manual_seed(99)
     latents = [torch.randn(i, DIM, device=dev, generator=gen).to(torch.bfloat16) for i, _ in spec]
@@ -636,6 +642,8 @@ def run_train(args: argparse.Namespace) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # each rank's pinned offload ring on the NUMA node of its GPU (host-DRAM traffic of N offload streams)
+    numa_cpus = ao.bind_to_device_numa_node(dev) if not args.no_numa_bind else None
     if world > 1:
         import datetime
 
@@ -652,6 +660,7 @@ def run_train(args: argparse.Namespace) -> None:
         streamer = model.block_swap_manager
         torch.cuda.empty_cache()
     model.activation_offload = not args.no_offload
+    model.activation_offload_defer_bytes = args.offload_defer_mb << 20
     params = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
     reducer = GradAllReducer(params, timing=True)
@@ -835,10 +844,12 @@ def run_train(args: argparse.Namespace) -> None:
                     "d2h_bytes_per_step": 4},
             "roofline": roofline,
             "gemm_tflops": gemm_tflops,
-            "offload": {"bytes_per_step": offload_bytes / args.steps,
+            "offload": {"bytes_per_step": offload_bytes / args.steps, "defer_bytes": args.offload_defer_mb << 20,
                         "gbs_over_step": offload_bytes / (elapsed_ms * 1e-3) / 1e9,
                         "pinned_bytes": stats1["pinned_bytes"]},
             "clocks": clock_info,
+            "host_binding": {"cpus": len(numa_cpus) if numa_cpus else None,
+                             "note": "rank 0's CPU affinity: the cores NVML reports local to its GPU (None: not bound)"},
             "gpu_launches": launches + sum(other_launches.values()),
             "gpu_launches_by_kind": {"int8_gemm": launches, **other_launches},
             "gpu_launches_note": ("libmoss_w8.so kernel launches in the timed region: int8 GEMM calls (fwd + dx; "

@@ -98,6 +98,38 @@ def _c_contiguous(shape: tuple[int, ...], stride: tuple[int, ...]) -> bool:
     return True
 
 
+def bind_to_device_numa_node(device: torch.device) -> list[int] | None:
+    """Restrict this process to the CPU cores NVML reports as local to ``device``.
+
+    Call it once per rank, before the first offload: the offload ring's pinned host memory is
+    then allocated (and first touched) on the NUMA node next to the GPU's PCIe root, so the
+    copy engines of the GPUs of a multi-socket host write to local memory instead of crossing
+    the socket interconnect. Reads the affinity only (no GPU setting changes); returns the
+    cores, or ``None`` when NVML or the affinity query is unavailable (nothing is changed).
+    """
+    try:
+        import pynvml
+    except ImportError:
+        return None
+    props = torch.cuda.get_device_properties(device)
+    bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    ncpu = os.cpu_count() or 1
+    try:
+        pynvml.nvmlInit()
+        handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (ncpu + 63) // 64)
+    except Exception:  # NVML missing on the host, or the query is not supported
+        return None
+    cpus = [64 * i + b for i, word in enumerate(words) for b in range(64) if (int(word) >> b) & 1 and 64 * i + b < ncpu]
+    if not cpus:
+        return None
+    try:
+        os.sched_setaffinity(0, cpus)
+    except OSError:
+        return None
+    return cpus
+
+
 def _host_memory_bytes() -> int:
     try:
         return os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES")
@@ -202,10 +234,14 @@ def offload_ring(device: torch.device) -> OffloadRing:
 
 
 class _OffloadedTensor:
-    """A saved activation living in the pinned ring (reference fields plus a ticket)."""
+    """A saved activation living in the pinned ring (reference fields plus a ticket).
+
+    While its copy is deferred (the most recently saved tensors, see ``defer_bytes``) it has no
+    ticket and ``resident`` holds the saved tensor itself.
+    """
 
     __slots__ = ("ring", "ticket", "device", "dtype", "shape", "stride", "payload_shape", "nbytes", "index",
-                 "restored", "__weakref__")
+                 "restored", "resident", "deferred", "__weakref__")
 
     def __init__(self, ring, ticket, device, dtype, shape, stride, payload_shape, nbytes, index):
         self.ring = ring
@@ -218,6 +254,8 @@ class _OffloadedTensor:
         self.nbytes = nbytes
         self.index = index
         self.restored: torch.Tensor | None = None
+        self.resident: torch.Tensor | None = None
+        self.deferred = False  # counted in its scope's deferred bytes
 
     def __del__(self):
         ring, ticket = self.ring, self.ticket
@@ -230,20 +268,43 @@ class _OffloadedTensor:
 
 
 class _OffloadScope:
-    """Book-keeping of one forward: saved tensors in pack order and restore prefetch."""
+    """Book-keeping of one forward: saved tensors in pack order, deferred copies and restore
+    prefetch."""
 
-    def __init__(self, ring: OffloadRing, prefetch_bytes: int) -> None:
+    def __init__(self, ring: OffloadRing, prefetch_bytes: int, defer_bytes: int = 0) -> None:
         self.ring = ring
         self.prefetch_bytes = prefetch_bytes
+        self.defer_bytes = defer_bytes
         self.entries: list[weakref.ref] = []
         self.next_scan = -1  # next pack index to consider for prefetch (walks downwards)
         self.in_flight = 0
         self.lock = threading.Lock()
         self.packed_bytes = 0
+        self.deferred: list[weakref.ref] = []  # saved, not copied yet, oldest first
+        self.deferred_bytes = 0
 
     def add(self, entry: _OffloadedTensor) -> None:
         self.entries.append(weakref.ref(entry))
         self.packed_bytes += entry.nbytes
+
+    def defer(self, entry: _OffloadedTensor, offload) -> None:
+        """Keep `entry` resident for now; copy out the oldest deferred tensors beyond the budget.
+
+        Backward needs the saved tensors in reverse order, so the newest ones are needed first:
+        copying them out would only bring them straight back, and on a shared host link their
+        copies would queue behind every earlier one.
+        """
+        with self.lock:
+            entry.deferred = True
+            self.deferred.append(weakref.ref(entry))
+            self.deferred_bytes += entry.nbytes
+            while self.deferred_bytes > self.defer_bytes and self.deferred:
+                oldest = self.deferred.pop(0)()
+                if oldest is None or not oldest.deferred:
+                    continue
+                oldest.deferred = False
+                self.deferred_bytes -= oldest.nbytes
+                offload(oldest)
 
     def _issue(self, entry: _OffloadedTensor) -> None:
         ring = self.ring
@@ -258,6 +319,13 @@ class _OffloadScope:
 
     def restore(self, entry: _OffloadedTensor) -> torch.Tensor:
         with self.lock:
+            if entry.resident is not None:  # never copied out: hand back the saved tensor itself
+                resident = entry.resident
+                entry.resident = None
+                if entry.deferred:
+                    entry.deferred = False
+                    self.deferred_bytes -= entry.nbytes
+                return resident
             if entry.restored is None:
                 self._issue(entry)
             # Prefetch the tensors packed before this one (backward walks blocks in reverse).
@@ -304,12 +372,17 @@ def activation_cpu_offload(
     device: torch.device,
     *,
     prefetch_bytes: int | None = None,
+    defer_bytes: int | None = None,
 ) -> ContextManager[object]:
     """Offload tensors saved by autograd to the pinned host ring.
 
     Reference: training/activation_offload.py:80-149 (same arguments, same resident-set
     rules, CPU no-op). ``prefetch_bytes`` (default: ``model.activation_offload_prefetch_bytes``
-    or 256 MiB) bounds the restores kept in flight ahead of backward.
+    or 256 MiB) bounds the restores kept in flight ahead of backward. ``defer_bytes`` (default:
+    ``model.activation_offload_defer_bytes`` or 0, the reference's behaviour) keeps up to that
+    many bytes of the most recently saved tensors on the GPU, copying a tensor out only once
+    newer ones push it past the budget: the tensors backward needs first are then never sent
+    out and back. Every tensor's bytes are the same either way.
     """
     if not enabled or device.type != "cuda" or not torch.is_grad_enabled():
         return nullcontext()
@@ -333,18 +406,16 @@ def activation_cpu_offload(
     if prefetch_bytes is None:
         prefetch_bytes = int(getattr(model, "activation_offload_prefetch_bytes", DEFAULT_PREFETCH_BYTES))
     scope_device = device if device.index is not None else torch.device("cuda", torch.cuda.current_device())
-    scope = _OffloadScope(offload_ring(scope_device), prefetch_bytes)
+    if defer_bytes is None:
+        defer_bytes = int(getattr(model, "activation_offload_defer_bytes", 0))
+    scope = _OffloadScope(offload_ring(scope_device), prefetch_bytes, defer_bytes)
 
-    def pack(tensor: torch.Tensor):
-        if tensor.device.type != "cuda" or is_weight_backed(tensor) or getattr(tensor, KEEP_RESIDENT, False):
-            return tensor
-        view = _offload_view(tensor)
-        if view is None:
-            return tensor
-        source, payload_shape = view
-        ring = scope.ring if tensor.device == scope.ring.device else offload_ring(tensor.device)
+    def copy_out(entry: _OffloadedTensor, tensor: torch.Tensor, source: torch.Tensor) -> bool:
+        """Issue the D2H copy of a saved tensor's payload; False when the ring is full."""
+        ring = entry.ring
         compute = torch.cuda.current_stream(tensor.device)
-        nbytes = source.numel() * source.element_size()
+        nbytes = entry.nbytes
+        payload_shape = entry.payload_shape
         if source.is_contiguous():
             staged = source
         else:
@@ -357,11 +428,37 @@ def activation_cpu_offload(
             _lib.count_launch("strided_copy")
         ticket = ring.pack(staged.data_ptr(), nbytes, compute)
         if ticket is None:  # ring at its limit: keep this tensor resident, like other exclusions
-            return tensor
+            return False
         staged.record_stream(ring.d2h_stream)
+        entry.ticket = ticket
+        return True
+
+    def deferred_copy_out(entry: _OffloadedTensor) -> None:
+        tensor = entry.resident
+        view = _offload_view(tensor)
+        if view is not None and copy_out(entry, tensor, view[0]):
+            entry.resident = None
+        # else: stays resident (ring full); restore() hands the tensor back
+
+    def pack(tensor: torch.Tensor):
+        if tensor.device.type != "cuda" or is_weight_backed(tensor) or getattr(tensor, KEEP_RESIDENT, False):
+            return tensor
+        view = _offload_view(tensor)
+        if view is None:
+            return tensor
+        source, payload_shape = view
+        ring = scope.ring if tensor.device == scope.ring.device else offload_ring(tensor.device)
+        nbytes = source.numel() * source.element_size()
         own = ring is scope.ring
-        entry = _OffloadedTensor(ring, ticket, tensor.device, tensor.dtype, tuple(tensor.shape),
+        entry = _OffloadedTensor(ring, None, tensor.device, tensor.dtype, tuple(tensor.shape),
                                  tuple(tensor.stride()), payload_shape, nbytes, len(scope.entries) if own else -1)
+        if own and scope.defer_bytes > 0:
+            entry.resident = tensor
+            scope.add(entry)
+            scope.defer(entry, deferred_copy_out)
+            return (entry, scope)
+        if not copy_out(entry, tensor, source):
+            return tensor
         if own:
             scope.add(entry)
         return (entry, scope if own else None)

@@ -206,3 +206,53 @@ def test_offload_matches_resident_on_int8_lora_model(cuda_device):
     assert torch.equal(results[0][0], results[1][0])
     for a, b in zip(results[0][1], results[1][1]):
         assert torch.equal(a, b)
+
+
+def test_deferred_copies_keep_the_newest_tensors_and_gradients_identical(cuda_device):
+    """With a deferral budget the newest saved tensors stay on the GPU (never copied out and
+    back) and only the older ones go through the ring; the gradients are bit-identical to the
+    run without offload for every budget, and the bytes copied shrink as the budget grows."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from moss_image_b200.dit import build_lora_model, flow_matching_loss
+
+    torch.manual_seed(0)
+    model = build_lora_model(3, device=cuda_device, dim=256, heads=2, mlp_dim=512, rank=8, seed=4)
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.requires_grad:
+                p.add_(torch.randn_like(p) * 0.02)
+    gen = torch.Generator(device=cuda_device).manual_seed(2)
+    latents = torch.randn(2, 96, 256, device=cuda_device, generator=gen).to(torch.bfloat16)
+    text = torch.randn(2, 32, 256, device=cuda_device, generator=gen).to(torch.bfloat16)
+    noise = torch.randn(2, 96, 256, device=cuda_device, generator=gen).to(torch.bfloat16)
+    t = torch.rand(2, device=cuda_device, generator=gen)
+    ring = ao.offload_ring(cuda_device)
+    block_input = 2 * 128 * 256 * 2  # one checkpointed block's saved input
+
+    def run(offload: bool, defer_bytes: int):
+        model.activation_offload = offload
+        model.activation_offload_defer_bytes = defer_bytes
+        before = ring.stats()["d2h_bytes"]
+        with sdpa_kernel(SDPBackend.MATH):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = flow_matching_loss(model, latents, text, t, noise)
+            loss.backward()
+        torch.cuda.synchronize()
+        grads = [p.grad.clone() for p in model.parameters() if p.requires_grad]
+        model.zero_grad(set_to_none=True)
+        return loss.detach().clone(), grads, ring.stats()["d2h_bytes"] - before
+
+    reference = run(False, 0)
+    moved = []
+    for budget in (0, 3 * block_input, 1 << 40):
+        loss, grads, nbytes = run(True, budget)
+        assert torch.equal(loss, reference[0])
+        for a, b in zip(grads, reference[1]):
+            assert torch.equal(a, b)
+        moved.append(nbytes)
+    model.activation_offload_defer_bytes = 0
+    assert moved[0] >= 3 * block_input  # every block input goes out
+    assert 0 < moved[1] <= moved[0] - 2 * block_input  # the newest ~3 block inputs' worth stays
+    assert moved[2] == 0  # everything stays
+    assert ring.stats()["live"] == 0
