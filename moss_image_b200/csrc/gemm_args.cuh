@@ -40,6 +40,8 @@ struct Args {
   // ConvRot grad-input (CTA-pair kernel only): rotate each output row by the grouped Hadamard
   // transform of this group size in the epilogue; 0 = no rotation.
   int rot_group;
+  // CTA-pair kernel: row tiles per rasterisation group (tile_coords)
+  int group_m;
 };
 
 // k-block schedule of one work unit: iteration i -> weight k-block or LoRA block.
@@ -111,11 +113,12 @@ inline bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const 
 // blocks, so the tiles in flight at one time (one per CTA or CTA pair) cover a compact
 // block of the output and reuse their A rows and weight columns from L2.
 constexpr int kGroupM = 8;
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m_blk, int& n_blk) {
-  const int per_group = kGroupM * tiles_n;
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m_blk, int& n_blk,
+                                            int group_m = kGroupM) {
+  const int per_group = group_m * tiles_n;
   const int group = t / per_group;
-  const int first_m = group * kGroupM;
-  const int gsm = min(tiles_m - first_m, kGroupM);
+  const int first_m = group * group_m;
+  const int gsm = min(tiles_m - first_m, group_m);
   const int r = t - group * per_group;
   m_blk = first_m + r % gsm;
   n_blk = r / gsm;

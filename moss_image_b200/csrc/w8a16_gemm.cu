@@ -667,6 +667,7 @@ static int run(bool dx, const void* a_ptr, int v_kind, int64_t M, int64_t Kr, in
   a.tail_first = a.tiles_m * a.tiles_n;  // the CTA-pair kernel's last-round split: none
   a.tail_splits = 1;
   a.rot_group = 0;
+  a.group_m = kGroupM;
 
   CUtensorMap ta, tw, te;
   memset(&ta, 0, sizeof(ta));

@@ -142,6 +142,20 @@ __device__ __forceinline__ float* partial_at(const Args& a, int tail, int split,
   return a.partial + ((static_cast<int64_t>(tail) * a.tail_splits + split) * kTileM + lrow) * kTileN + lcol;
 }
 
+// L2 policy for the output stores: evict first. The outputs are written once and read by the
+// next operation, while the A rows and weight columns are re-read by later tiles; without the
+// hint a 12288-wide output streaming through L2 evicts the weight between row groups.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+__device__ __forceinline__ void stg256_evict_first(void* p, const uint32_t (&v)[8], uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(p), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "l"(policy)
+               : "memory");
+}
+
 // Bias (forward) and the rounded store of 32 consecutive outputs of one row.
 template <bool kDX, int kV>
 __device__ __forceinline__ void store_out32(const Args& args, float (&v)[32], int row, int col0, bool vec_ok) {
@@ -163,8 +177,9 @@ __device__ __forceinline__ void store_out32(const Args& args, float (&v)[32], in
       p1[j] = pack2_kind<kV>(v[16 + 2 * j], v[16 + 2 * j + 1]);
     }
     uint16_t* dst = static_cast<uint16_t*>(args.out) + off;
-    stg256(dst, p0);
-    stg256(dst + 16, p1);
+    const uint64_t policy = l2_evict_first_policy();
+    stg256_evict_first(dst, p0, policy);
+    stg256_evict_first(dst + 16, p1, policy);
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
@@ -186,7 +201,7 @@ __global__ void __launch_bounds__(256) pair_tail_reduce_kernel(const Args args) 
     const int lrow = static_cast<int>((i / kQuads) % kTileM);
     const int tail = static_cast<int>(i / (static_cast<int64_t>(kQuads) * kTileM));
     int m_blk, n_blk;
-    tile_coords(args.tail_first + tail, args.tiles_m, args.tiles_n, m_blk, n_blk);
+    tile_coords(args.tail_first + tail, args.tiles_m, args.tiles_n, m_blk, n_blk, args.group_m);
     const int row = m_blk * kTileM + lrow;
     const int col = n_blk * kTileN + quad * 4;
     if (row >= args.M || col >= args.Nc) continue;
@@ -421,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = pair_id; u < num_units && ok; u += num_pairs) {
       const Unit w = unit_of(args, u, nsteps);
       int m_blk, n_blk;
-      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk, args.group_m);
       const int m0 = m_blk * kTileM + static_cast<int>(rank) * kHalf;
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
       for (int si = w.s0; si < w.s1; ++si) {
@@ -567,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       tc_fence_after();
       int m_blk, n_blk;
-      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk, args.group_m);
       const int lrow = static_cast<int>(rank) * kHalf + q * 32 + lane;  // row within the tile
       const int row = m_blk * kTileM + lrow;
       const int n0 = n_blk * kTileN;
@@ -645,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (!kDX) {
         const bool valid = u_next < num_units;
         int mb = 0, nb = 0;
-        if (valid) tile_coords(unit_of(args, u_next, nsteps).tile, args.tiles_m, args.tiles_n, mb, nb);
+        if (valid) tile_coords(unit_of(args, u_next, nsteps).tile, args.tiles_m, args.tiles_n, mb, nb, args.group_m);
         const int base_n = nb * kTileN + static_cast<int>(rank) * kHalf;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -658,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = pair_id; u < num_units && ok; u += num_pairs) {
       const Unit w = unit_of(args, u, nsteps);
       int m_blk, n_blk;
-      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk);
+      tile_coords(w.tile, args.tiles_m, args.tiles_n, m_blk, n_blk, args.group_m);
       const int n0 = n_blk * kTileN + static_cast<int>(rank) * kHalf;
       Dec<kV, kFast> dec_f[8];
       if constexpr (!kDX) {
@@ -885,8 +900,17 @@ PairTailPlan plan_pair_tail(int64_t M, int64_t Nc, int64_t Kr, int sms) {
   return p;
 }
 
-int launch_pair(bool dx, int v_kind, bool fast, const Args& a, cudaStream_t s) {
+int launch_pair(bool dx, int v_kind, bool fast, const Args& a_in, cudaStream_t s) {
   using namespace pair;
+  Args a = a_in;
+  // Rasterisation: groups of row tiles x all column tiles. With few column tiles, a group of 8
+  // rows spans more than one round of the persistent grid, and the tiles of the next round
+  // stream the same A rows from DRAM again (2.9x the A bytes at K = 12288, N = 3072); a group
+  // of at most one round's worth of tiles keeps each A row block within one round.
+  {
+    const int pairs = std::max(1, sm_count() / 2);
+    a.group_m = a.tiles_n < pairs ? std::max(1, std::min(kGroupM, pairs / a.tiles_n)) : kGroupM;
+  }
   // A: [M, Kr] viewed as {64, M, Kr / 64} so one box carries kSub k-blocks of 128 rows.
   if (a.Kr % BK != 0) return MOSS_ERR_UNSUPPORTED;
   const CUtensorMapDataType v_dt = v_kind == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
