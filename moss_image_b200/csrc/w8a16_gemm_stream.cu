@@ -56,7 +56,10 @@ constexpr int kDxSlab = 16;      // reduction rows per grad-input slab
 #endif
 constexpr int kFwdBatch = MOSS_STREAM_FWD_BATCH;
 constexpr int kDxBatch = 2;
-constexpr int kMinCtasPerSm = 3;  // register budget: 65536 / (3 x 256) = 85 per thread
+#ifndef MOSS_STREAM_MIN_CTAS
+#define MOSS_STREAM_MIN_CTAS 3
+#endif
+constexpr int kMinCtasPerSm = MOSS_STREAM_MIN_CTAS;  // register budget: 65536 / (3 x 256) = 85 per thread
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
