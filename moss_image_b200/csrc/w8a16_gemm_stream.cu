@@ -44,12 +44,13 @@ constexpr int kFwdRows = 16;     // output features per forward CTA
 constexpr int kFwdSlab = 64;     // reduction elements per forward slab (16 codes per lane x 4 lanes)
 constexpr int kDxCols = 128;     // output columns per grad-input CTA
 constexpr int kDxSlab = 16;      // reduction rows per grad-input slab
-// Slabs whose weight loads a warp issues before it decodes any of them: 4 x 1 KB (forward) or
-// 2 x 2 KB (grad-input) per warp. With at most 80 registers per thread three CTAs fit on an SM,
-// so ~96 KB (forward) of weight loads are in flight per SM. (6 slabs per batch measured
-// slower on the long-K shapes: fewer CTAs fit and the batches of a CTA serialise.)
+// Slabs whose weight loads a warp issues before it decodes any of them: 3 x 1 KB (forward) or
+// 2 x 2 KB (grad-input) per warp. The forward's 64-register budget fits four CTAs (32 warps)
+// per SM, ~96 KB of weight loads in flight. Measured on the forward shapes (CUDA-graph timed,
+// 2 x 3072 -> 18432): 3 slabs x 4 CTAs 14.7 us, 4 x 3 16.5 us, 2 x 5 15.9 us, 6 x 2 19.2 us;
+// a per-warp cp.async ring of 4-8 slabs in shared memory instead of registers, 16.5-17.3 us.
 #ifndef MOSS_STREAM_FWD_BATCH
-#define MOSS_STREAM_FWD_BATCH 4
+#define MOSS_STREAM_FWD_BATCH 3
 #endif
 #ifndef MOSS_STREAM_CTAS_PER_SM
 #define MOSS_STREAM_CTAS_PER_SM 2
@@ -57,9 +58,9 @@ constexpr int kDxSlab = 16;      // reduction rows per grad-input slab
 constexpr int kFwdBatch = MOSS_STREAM_FWD_BATCH;
 constexpr int kDxBatch = 2;
 #ifndef MOSS_STREAM_MIN_CTAS
-#define MOSS_STREAM_MIN_CTAS 3
+#define MOSS_STREAM_MIN_CTAS 4
 #endif
-constexpr int kMinCtasPerSm = MOSS_STREAM_MIN_CTAS;  // register budget: 65536 / (3 x 256) = 85 per thread
+constexpr int kMinCtasPerSm = MOSS_STREAM_MIN_CTAS;  // register budget: 65536 / (4 x 256) = 64 per thread
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
