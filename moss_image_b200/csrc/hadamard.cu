@@ -241,32 +241,57 @@ __device__ __forceinline__ void smem_phase(float* tile, int nrows) {
   __syncthreads();
 }
 
-// Five CTAs per SM (48 registers): occupancy hides the load latency better than a
-// register-held prefetch of the next tile, which measured slower.
+// The tensor is contiguous [rows, cols] with cols a multiple of the group, so its flat view is
+// a sequence of whole groups: a tile is kFastTile consecutive elements (kFastTile / group
+// groups), and the last tile holds the remaining whole groups. Each thread owns 16 consecutive
+// elements of a tile (32 bytes). The input is prefetched kPipe - 1 tiles ahead with cp.async
+// into a per-thread slot of a shared ring (a thread reads back only what it copied, so the ring
+// needs no barrier), keeping 2 x 8 KB per CTA in flight while the current tile is rotated.
+constexpr int kPipe = 3;
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <int kKind, int LOG2G>
 __global__ void __launch_bounds__(kThreads, 5)
-    hadamard_fast_kernel(const uint16_t* x, uint16_t* y, int64_t rows, int64_t cols) {
-  constexpr int kGroup = 1 << LOG2G;
+    hadamard_fast_kernel(const uint16_t* x, uint16_t* y, int64_t total) {
   constexpr int kPhases = (LOG2G + 3) / 4;
-  constexpr int kRowsPerTile = kFastTile >> LOG2G;
   __shared__ float tile[kPhases > 1 ? kFastTile + kFastTile / 16 : 1];
-  const int64_t groups_per_row = cols >> LOG2G;
-  const int64_t row_tiles = (rows + kRowsPerTile - 1) / kRowsPerTile;
-  const int64_t tiles = row_tiles * groups_per_row;
+  __shared__ __align__(16) uint4 ring[kPipe][kThreads * 2];
+  const int64_t tiles = (total + kFastTile - 1) / kFastTile;
   const int t = threadIdx.x;
-  for (int64_t tix = blockIdx.x; tix < tiles; tix += gridDim.x) {
-    const int64_t row0 = (tix / groups_per_row) * kRowsPerTile;
-    const int64_t col0 = (tix % groups_per_row) << LOG2G;
-    const int nrows = static_cast<int>(std::min<int64_t>(kRowsPerTile, rows - row0));
-    // phase 0: 16 contiguous elements of one row straight from global memory
+  const int e0 = t * 16;  // element index within the tile (row-major groups)
+  // copy this thread's 32 bytes of the j-th tile of this CTA into ring slot j % kPipe
+  auto prefetch = [&](int64_t j) {
+    const int64_t tix = blockIdx.x + j * gridDim.x;
+    if (tix < tiles && tix * kFastTile + e0 < total) {
+      const uint16_t* src = x + tix * kFastTile + e0;
+      const uint32_t dst = smem_u32(&ring[j % kPipe][2 * t]);
+      cp_async16(dst, src);
+      cp_async16(dst + 16, src + 8);
+    }
+    cp_async_commit();  // empty groups keep the group count uniform
+  };
+#pragma unroll
+  for (int j = 0; j < kPipe - 1; ++j) prefetch(j);
+  int64_t j = 0;
+  for (int64_t tix = blockIdx.x; tix < tiles; tix += gridDim.x, ++j) {
+    prefetch(j + kPipe - 1);  // into the slot read in the previous iteration
+    cp_async_wait<kPipe - 1>();
+    const int64_t base = tix * kFastTile;
+    const int count = static_cast<int>(std::min<int64_t>(kFastTile, total - base));  // whole groups
+    const int nrows = count >> LOG2G;
+    // phase 0: the thread's 16 contiguous elements, from its ring slot
     float v[16];
-    const int e0 = t * 16;  // element index within the tile (row-major rows of the group)
-    const int r0 = e0 >> LOG2G;
-    const bool live = r0 < nrows;
-    uint16_t* dst_row = y + (row0 + r0) * cols + col0 + (e0 & (kGroup - 1));
+    const bool live = e0 < count;
     if (live) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r0) * cols + col0 + (e0 & (kGroup - 1)));
-      const uint4 u0 = src[0], u1 = src[1];
+      const uint4 u0 = ring[j % kPipe][2 * t], u1 = ring[j % kPipe][2 * t + 1];
       const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -307,28 +332,29 @@ __global__ void __launch_bounds__(kThreads, 5)
           memcpy(&w[k], &h2, sizeof(uint32_t));
         }
       }
-      uint4* dst = reinterpret_cast<uint4*>(dst_row);
+      uint4* dst = reinterpret_cast<uint4*>(y + base + e0);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
       dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
     }
     if constexpr (kPhases > 1) __syncthreads();  // the next tile reuses the shared memory
   }
+  cp_async_wait<0>();  // no copy outlives the CTA (the trailing groups are empty)
 }
 
 template <int kKind>
-void launch_fast(const void* x, void* y, int64_t rows, int64_t cols, int log2g, unsigned grid, cudaStream_t s) {
+void launch_fast(const void* x, void* y, int64_t total, int log2g, unsigned grid, cudaStream_t s) {
   const uint16_t* xi = static_cast<const uint16_t*>(x);
   uint16_t* yi = static_cast<uint16_t*>(y);
   switch (log2g) {
-    case 4: hadamard_fast_kernel<kKind, 4><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 5: hadamard_fast_kernel<kKind, 5><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 6: hadamard_fast_kernel<kKind, 6><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 7: hadamard_fast_kernel<kKind, 7><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 8: hadamard_fast_kernel<kKind, 8><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 9: hadamard_fast_kernel<kKind, 9><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 10: hadamard_fast_kernel<kKind, 10><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    case 11: hadamard_fast_kernel<kKind, 11><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
-    default: hadamard_fast_kernel<kKind, 12><<<grid, kThreads, 0, s>>>(xi, yi, rows, cols); break;
+    case 4: hadamard_fast_kernel<kKind, 4><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 5: hadamard_fast_kernel<kKind, 5><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 6: hadamard_fast_kernel<kKind, 6><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 7: hadamard_fast_kernel<kKind, 7><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 8: hadamard_fast_kernel<kKind, 8><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 9: hadamard_fast_kernel<kKind, 9><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 10: hadamard_fast_kernel<kKind, 10><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    case 11: hadamard_fast_kernel<kKind, 11><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
+    default: hadamard_fast_kernel<kKind, 12><<<grid, kThreads, 0, s>>>(xi, yi, total); break;
   }
 }
 
@@ -370,13 +396,13 @@ extern "C" int moss_hadamard_rotate(const void* x, int dtype, int64_t rows, int6
   if (fast_ok) {
     int log2g = 0;
     while ((int64_t{1} << log2g) < group) ++log2g;
-    const int64_t rows_per_tile = kFastTile / group;
-    const int64_t tiles = (rows + rows_per_tile - 1) / rows_per_tile * (cols / group);
-    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, 8LL * sm_count())));
+    const int64_t total = rows * cols;
+    const int64_t tiles = (total + kFastTile - 1) / kFastTile;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(tiles, 5LL * sm_count())));
     if (dtype == kBF16)
-      launch_fast<kBF16>(x, y, rows, cols, log2g, grid, s);
+      launch_fast<kBF16>(x, y, total, log2g, grid, s);
     else
-      launch_fast<kF16>(x, y, rows, cols, log2g, grid, s);
+      launch_fast<kF16>(x, y, total, log2g, grid, s);
     MOSS_CUDA_TRY(cudaGetLastError());
     return clear_ok();
   }

@@ -33,7 +33,7 @@ def _np(t: torch.Tensor) -> np.ndarray:
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("group", [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 8192])
+@pytest.mark.parametrize("group", [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192])
 def test_rotation_kernel_is_bit_exact_with_the_oracle(cuda_device, dtype, group):
     rows = 37
     cols = max(group, 256) * 2
