@@ -442,6 +442,9 @@ def graph_time_us(calls, device, reps: int | None = None) -> float:
     import torch
 
     stream = torch.cuda.Stream(device)
+    # the inputs were produced on the current stream, and freed temporaries of that stream may
+    # back the outputs: the side stream starts only after that work
+    torch.cuda.synchronize(device)
     with torch.cuda.stream(stream):
         for call in calls:  # one-time set-up (attributes, symbol lookups) outside the capture
             call()

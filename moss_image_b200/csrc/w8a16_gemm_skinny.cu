@@ -60,24 +60,14 @@ constexpr int kMaxXStages = 4;
 
 // Shared-memory budget per token-tile width: narrow tiles fetch kSub activation k-blocks per
 // copy (a tensor copy costs a roughly fixed ~500 cycles), wide ones one k-block per copy.
-#ifndef MOSS_SKINNY_X128_SUB
-#define MOSS_SKINNY_X128_SUB 1
-#endif
-#ifndef MOSS_SKINNY_X128_STAGES
-#define MOSS_SKINNY_X128_STAGES 4
-#endif
-#ifndef MOSS_SKINNY_C128_STAGES
-#define MOSS_SKINNY_C128_STAGES 6
-#endif
-__host__ __device__ constexpr int x_sub_of(int nt) { return nt <= 64 ? kSub : nt == 128 ? MOSS_SKINNY_X128_SUB : 1; }
 template <int kNT>
 struct Cfg {
-  static constexpr int kXSub = x_sub_of(kNT);
+  static constexpr int kXSub = kNT <= 64 ? kSub : 1;
   static constexpr int kWStages = kNT <= 32 ? 3 : 2;
-  static constexpr int kXStages = kNT == 128 ? MOSS_SKINNY_X128_STAGES : 2;
+  static constexpr int kXStages = kNT == 128 ? 4 : 2;
   // More converted stages than converter groups: a group then never waits for the MMA of its
   // own previous k-block before converting the next one.
-  static constexpr int kCStages = kNT == 16 ? 7 : kNT == 128 ? MOSS_SKINNY_C128_STAGES : 6;
+  static constexpr int kCStages = kNT == 16 ? 7 : 6;
   static constexpr uint32_t kXBlock = kNT * BK * 2;  // one k-block of kNT activation rows
   static constexpr uint32_t kXStage = kXSub * kXBlock;
   static constexpr uint32_t kDataBytes = kWStages * kWStage + kXStages * kXStage + kCStages * kCBlock;
@@ -674,7 +664,7 @@ int launch_skinny(bool dx, int v_kind, bool fast, int nt, const Args& a, cudaStr
     // activations [M, Kr] viewed as {64, M, Kr / 64}: one box = kSub (nt <= 64) or 1 k-blocks of nt rows
     const uint64_t dims[3] = {BK, static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.Kr / BK)};
     const uint64_t strides[2] = {static_cast<uint64_t>(a.lda) * 2, BK * 2};
-    const uint32_t box[3] = {BK, static_cast<uint32_t>(nt), static_cast<uint32_t>(x_sub_of(nt))};
+    const uint32_t box[3] = {BK, static_cast<uint32_t>(nt), nt <= 64 ? static_cast<uint32_t>(kSub) : 1u};
     if (!make_map_nd(&tx, v_dt, 2, a.a, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return MOSS_ERR_UNSUPPORTED;
   }
   if (!dx) {

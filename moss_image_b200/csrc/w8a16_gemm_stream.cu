@@ -56,16 +56,7 @@ constexpr int kDxSlab = 16;      // reduction rows per grad-input slab
 #define MOSS_STREAM_CTAS_PER_SM 2
 #endif
 constexpr int kFwdBatch = MOSS_STREAM_FWD_BATCH;
-#ifndef MOSS_STREAM_DX_BATCH
-#define MOSS_STREAM_DX_BATCH 2
-#endif
-#ifndef MOSS_STREAM_DX_MIN_CTAS
-#define MOSS_STREAM_DX_MIN_CTAS 1
-#endif
-#ifndef MOSS_STREAM_DX_CTAS_PER_SM
-#define MOSS_STREAM_DX_CTAS_PER_SM 2
-#endif
-constexpr int kDxBatch = MOSS_STREAM_DX_BATCH;
+constexpr int kDxBatch = 2;
 #ifndef MOSS_STREAM_MIN_CTAS
 #define MOSS_STREAM_MIN_CTAS 4
 #endif
@@ -260,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, kMT == 1 ? kMinCtasPerSm : 2) w8_str
 // grid = (Nc / 128) * splits; block = 256; dynamic shared memory = red. CTA b: output strip
 // b / splits (128 columns of dX), reduction split b % splits (slabs of 16 weight rows).
 template <int kV, bool kFast, int kMT>
-__global__ void __launch_bounds__(kThreads, kMT == 1 ? MOSS_STREAM_DX_MIN_CTAS : 1) w8_stream_dx_kernel(const Args a, int splits, int per_split) {
+__global__ void __launch_bounds__(kThreads) w8_stream_dx_kernel(const Args a, int splits, int per_split) {
   constexpr int kRedStride = kDxCols + 1;
   extern __shared__ float red_dyn[];  // [kWarps][8 * kMT][kRedStride]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -398,7 +389,7 @@ StreamPlan plan_stream(bool dx, int64_t M, int64_t Nc, int64_t Kr, int sms) {
     tiles = Nc / kDxCols;
     slabs = Kr / kDxSlab;
   }
-  const int64_t target = static_cast<int64_t>(dx ? MOSS_STREAM_DX_CTAS_PER_SM : MOSS_STREAM_CTAS_PER_SM) * sms;
+  const int64_t target = static_cast<int64_t>(MOSS_STREAM_CTAS_PER_SM) * sms;
   int64_t splits = std::min<int64_t>((target + tiles - 1) / tiles, std::max<int64_t>(1, slabs / kWarps));
   splits = std::max<int64_t>(1, splits);
   const int64_t per = (slabs + splits - 1) / splits;
