@@ -249,15 +249,6 @@ __device__ __forceinline__ void smem_phase(float* tile, int nrows) {
 // needs no barrier), keeping 2 x 8 KB per CTA in flight while the current tile is rotated.
 constexpr int kPipe = 3;
 
-__device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 template <int kKind, int LOG2G>
 __global__ void __launch_bounds__(kThreads, 5)
     hadamard_fast_kernel(const uint16_t* x, uint16_t* y, int64_t total) {
