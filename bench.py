@@ -475,17 +475,40 @@ def graph_time_us(calls, device, reps: int | None = None) -> float:
     return us
 
 
+def reference_triton_kernels():
+    """The reference's own Triton W8A16 kernels (training/quant_kernels.py:294-373), imported
+    from the reference package installed under baseline/_ref (pip --target, no deps). Returns
+    (module, None), or (None, why) when the install or Triton is missing."""
+    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_dir, "training", "quant_kernels.py")):
+        return None, "reference package not installed under baseline/_ref"
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        from training import quant_kernels as ref_qk
+    except Exception as error:  # the comparator is optional; the sweep still runs without it
+        return None, f"reference quant_kernels import failed: {error}"
+    if getattr(ref_qk, "triton", None) is None:
+        return None, "Triton is not importable"
+    return ref_qk, None
+
+
 def run_sweep(args: argparse.Namespace) -> None:
     """The W8A16 GEMM sweep (M x (K, N), forward and grad-input), one JSON line per shape.
 
-    Three implementations on the same GPU, each timed as back-to-back launches captured in a
+    Four implementations on the same GPU, each timed as back-to-back launches captured in a
     CUDA graph (device time only, no host launch latency):
     * ``ours``: this library's kernels through the C ABI, preallocated buffers and workspace;
+    * ``ref_triton``: the reference's own Triton kernels (``triton_int8_linear_forward`` /
+      ``_backward``, training/quant_kernels.py:294-373, 32 x 32 x 32 tiles), when the
+      reference package is installed under baseline/_ref, with preallocated outputs;
     * ``eager_gpu``: the reference's eager algorithm (decode ``q.to(bf16) * s.to(bf16)[:, None]``
       then ``F.linear`` / ``matmul`` on cuBLAS, training/quantization.py:23-24,43,61-64);
     * ``cublas_bf16``: a plain bf16 cuBLAS GEMM on a dense bf16 weight (the ceiling).
     Every launch reads its own copy of the weight, with enough copies that the weights touched
-    by one graph exceed twice the 126 MB L2: the weight stream is measured from HBM.
+    by one graph exceed twice the 126 MB L2: the weight stream is measured from HBM. Each cell
+    also reports the relative Frobenius difference between our output and the reference
+    Triton kernel's on the same inputs.
     """
     import ctypes
 
@@ -502,6 +525,9 @@ def run_sweep(args: argparse.Namespace) -> None:
     status = qk.status_buffer(dev)
     l2_cover = 320 << 20
     grid_m = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else [128, 512, 2048, 8192, 32768]
+    ref_qk, ref_missing = reference_triton_kernels()
+    if ref_missing:
+        print(json.dumps({"ref_triton": "unavailable", "why": ref_missing}), flush=True)
     for k, n in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072), (3072, 18432)]:
         copies = max(1, -(-l2_cover // (n * k)))
         dense_copies = max(1, -(-l2_cover // (2 * n * k)))
@@ -543,17 +569,35 @@ def run_sweep(args: argparse.Namespace) -> None:
                 def cublas(i, kind=kind):
                     return F.linear(x, dense[i]) if kind == "fwd" else dy.matmul(dense[i])
 
+                ref_out = torch.empty(m, n_out, device=dev, dtype=torch.bfloat16)
+
+                def ref_triton(i, kind=kind, ref_out=ref_out):
+                    if kind == "fwd":
+                        return ref_qk.triton_int8_linear_forward(x, qs[i], ss[i], None, torch.bfloat16, torch.bfloat16,
+                                                                 out=ref_out)
+                    return ref_qk.triton_int8_linear_backward(dy, qs[i], ss[i], torch.Size((m, k)), torch.bfloat16,
+                                                              torch.bfloat16, out=ref_out)
+
                 nbytes = n * k + 4 * n + 2 * m * k + 2 * m * n
                 t_roof = max(flops / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9))
                 entry = {}
-                for label, fn, count in (("ours", ours, copies), ("eager_gpu", eager, copies),
-                                         ("cublas_bf16", cublas, dense_copies)):
+                impls = [("ours", ours, copies), ("eager_gpu", eager, copies), ("cublas_bf16", cublas, dense_copies)]
+                if ref_qk is not None:
+                    impls.insert(1, ("ref_triton", ref_triton, copies))
+                for label, fn, count in impls:
                     us = graph_time_us([lambda i=i, fn=fn: fn(i) for i in range(count)], dev)
                     entry[label] = {"us": us, "tflops": flops / us / 1e6}
                 entry["ours"].update({"gbs": nbytes / entry["ours"]["us"] / 1e3,
                                       "roofline_frac": t_roof / (entry["ours"]["us"] * 1e-6)})
                 entry["speedup_vs_eager_gpu"] = entry["eager_gpu"]["us"] / entry["ours"]["us"]
                 entry["frac_of_cublas_bf16"] = entry["cublas_bf16"]["us"] / entry["ours"]["us"]
+                if ref_qk is not None:
+                    entry["speedup_vs_ref_triton"] = entry["ref_triton"]["us"] / entry["ours"]["us"]
+                    ours(0)
+                    ref_triton(0)
+                    mine = (y if kind == "fwd" else dx).float()
+                    theirs = ref_out.float()
+                    entry["rel_diff_vs_ref_triton"] = float((mine - theirs).norm() / theirs.norm().clamp_min(1e-30))
                 res[kind] = entry
                 del ws_owner
             res["roofline_peaks"] = f"max(flops / bf16_tflops, bytes / hbm_gbs) ({peak_kind})"
