@@ -76,6 +76,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--k", type=int, default=3072)
     p.add_argument("--n", type=int, default=3072)
     p.add_argument("--sweep", action="store_true")
+    p.add_argument("--ref-gpu-modules", action="store_true",
+                   help="the training step with the reference's own int8 linears (Triton backend), LoRA and "
+                        "activation offload from baseline/_ref swapped into the same model (1 GPU)")
     p.add_argument("--sweep-m", default=None, help="comma-separated M values of the sweep (default: the config grid)")
     return p.parse_args()
 
@@ -609,6 +612,119 @@ def run_sweep(args: argparse.Namespace) -> None:
     qk.check_device_status(dev)
 
 
+def swap_in_reference_modules(model, device) -> dict:
+    """Replace this library's hot-path modules in `model` with the reference's own, from the
+    reference package installed under baseline/_ref: every FrozenInt8Linear becomes
+    training.quantization.FrozenInt8Linear with the Triton backend (same int8 codes and scales,
+    copied), every LoRALinear becomes training.lora.LoRALinear (same adapter values), and the
+    stack's activation offload context becomes training.activation_offload.activation_cpu_offload.
+    The rest of the harness (norms, attention, elementwise) is unchanged."""
+    import torch
+    from torch import nn
+
+    ref_qk, missing = reference_triton_kernels()
+    if missing:
+        raise RuntimeError(f"reference modules unavailable: {missing}")
+    from training import activation_offload as ref_ao
+    from training.lora import LoRALinear as RefLoRA
+    from training.quantization import FrozenInt8Linear as RefInt8
+
+    from moss_image_b200 import dit
+    from moss_image_b200.lora import LoRALinear as OurLoRA
+    from moss_image_b200.quantization import FrozenInt8Linear as OurInt8
+
+    def ref_int8(mod):
+        dtype = mod.compute_dtype
+        linear = nn.Linear(mod.in_features, mod.out_features, bias=mod.bias is not None, device=device, dtype=dtype)
+        with torch.no_grad():
+            linear.weight.zero_()
+            if linear.bias is not None:
+                linear.bias.copy_(mod.bias)
+        linear.requires_grad_(False)
+        ref = RefInt8(linear, backend="triton")
+        with torch.no_grad():
+            ref.weight_int8.copy_(mod.weight_int8)
+            ref.weight_scale.copy_(mod.weight_scale)
+        return ref
+
+    counts = {"int8": 0, "lora": 0}
+    for name, parent in list(model.named_modules()):
+        for child_name, child in list(parent.named_children()):
+            if isinstance(child, OurLoRA) and isinstance(child.base, OurInt8):
+                wrapped = RefLoRA(ref_int8(child.base), child.rank, child.alpha).to(device)
+                with torch.no_grad():
+                    wrapped.lora_A.copy_(child.lora_A)
+                    wrapped.lora_B.copy_(child.lora_B)
+                setattr(parent, child_name, wrapped)
+                counts["lora"] += 1
+                counts["int8"] += 1
+            elif isinstance(child, OurInt8):
+                setattr(parent, child_name, ref_int8(child))
+                counts["int8"] += 1
+    dit.activation_cpu_offload = ref_ao.activation_cpu_offload
+    return counts
+
+
+def run_train_ref_modules(args: argparse.Namespace) -> None:
+    """One JSON line: the BASELINE config-3 step (same model, inputs, optimizer and offload
+    setting as the default run) with the reference's own hot-path modules swapped in, timed
+    the same way (CUDA events over `--steps` after `--warmup`, 1 GPU)."""
+    import torch
+
+    sys.path.insert(0, str(REPO))
+    from moss_image_b200.dit import build_lora_model, flow_matching_loss
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0,
+                             full_qkvo=args.full_qkvo)
+    swapped = swap_in_reference_modules(model, dev)
+    model.train()
+    model.activation_offload = not args.no_offload
+    params = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+    img_tokens, txt_tokens = args.img_tokens, args.txt_tokens
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    latents = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    text = torch.randn(args.batch, txt_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    noise = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    t = torch.rand(args.batch, device=dev, generator=gen)
+
+    def step() -> torch.Tensor:
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = flow_matching_loss(model, latents, text, t, noise)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    clocks = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        loss = step()
+    end.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    tokens = args.batch * (img_tokens + txt_tokens)
+    print(json.dumps({
+        "impl": "reference_gpu_modules",
+        "metric": "INT8-W DiT train tokens/s (reference modules on the same GPU)",
+        "value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": args.steps,
+        "warmup": args.warmup, "loss": float(loss.item()), "swapped": swapped,
+        "offload": not args.no_offload, "clocks": clock_info,
+        "note": "training.quantization.FrozenInt8Linear (backend triton), training.lora.LoRALinear and "
+                "training.activation_offload from baseline/_ref in place of this library's modules; "
+                "the rest of the synthetic model, the inputs and AdamW are the default run's",
+    }), flush=True)
+
+
 def run_packed(args: argparse.Namespace) -> None:
     """One training step over a heterogeneous batch: packed into one traversal (every GEMM sees
     all tokens, variable-length attention) versus one traversal per sample (what a batch of
@@ -930,6 +1046,8 @@ def main() -> None:
         run_kernel(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.ref_gpu_modules:
+        run_train_ref_modules(args)
     else:
         run_train(args)
 
