@@ -76,6 +76,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--k", type=int, default=3072)
     p.add_argument("--n", type=int, default=3072)
     p.add_argument("--sweep", action="store_true")
+    p.add_argument("--no-ref-gpu-arm", action="store_true",
+                   help="skip timing the step with the reference's own modules after a 1-GPU run")
     p.add_argument("--ref-gpu-modules", action="store_true",
                    help="the training step with the reference's own int8 linears (Triton backend), LoRA and "
                         "activation offload from baseline/_ref swapped into the same model (1 GPU)")
@@ -665,64 +667,74 @@ def swap_in_reference_modules(model, device) -> dict:
     return counts
 
 
-def run_train_ref_modules(args: argparse.Namespace) -> None:
-    """One JSON line: the BASELINE config-3 step (same model, inputs, optimizer and offload
-    setting as the default run) with the reference's own hot-path modules swapped in, timed
-    the same way (CUDA events over `--steps` after `--warmup`, 1 GPU)."""
+def time_reference_modules(args: argparse.Namespace, steps: int, warmup: int) -> dict:
+    """The BASELINE config-3 step (same model, inputs, optimizer and offload setting as the
+    default run) with the reference's own hot-path modules swapped in, timed the same way
+    (CUDA events over `steps` after `warmup`, 1 GPU). Returns the measurement."""
     import torch
 
     sys.path.insert(0, str(REPO))
+    from moss_image_b200 import dit
+    from moss_image_b200.activation_offload import activation_cpu_offload as ours_offload
     from moss_image_b200.dit import build_lora_model, flow_matching_loss
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     model = build_lora_model(args.depth, device=dev, dim=DIM, heads=HEADS, mlp_dim=MLP, rank=RANK, seed=0,
                              full_qkvo=args.full_qkvo)
-    swapped = swap_in_reference_modules(model, dev)
-    model.train()
-    model.activation_offload = not args.no_offload
-    params = [p for p in model.parameters() if p.requires_grad]
-    opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
-    img_tokens, txt_tokens = args.img_tokens, args.txt_tokens
-    gen = torch.Generator(device=dev).manual_seed(1234)
-    latents = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
-    text = torch.randn(args.batch, txt_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
-    noise = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
-    t = torch.rand(args.batch, device=dev, generator=gen)
+    try:
+        swapped = swap_in_reference_modules(model, dev)
+        model.train()
+        model.activation_offload = not args.no_offload
+        params = [p for p in model.parameters() if p.requires_grad]
+        opt = torch.optim.AdamW(params, lr=1e-4, fused=True)
+        img_tokens, txt_tokens = args.img_tokens, args.txt_tokens
+        gen = torch.Generator(device=dev).manual_seed(1234)
+        latents = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+        text = torch.randn(args.batch, txt_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+        noise = torch.randn(args.batch, img_tokens, DIM, device=dev, generator=gen).to(torch.bfloat16)
+        t = torch.rand(args.batch, device=dev, generator=gen)
 
-    def step() -> torch.Tensor:
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = flow_matching_loss(model, latents, text, t, noise)
-        loss.backward()
-        opt.step()
-        opt.zero_grad(set_to_none=True)
-        return loss.detach()
+        def step() -> torch.Tensor:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = flow_matching_loss(model, latents, text, t, noise)
+            loss.backward()
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            return loss.detach()
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    props = torch.cuda.get_device_properties(dev)
-    clocks = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
-    clocks.start()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        loss = step()
-    end.record()
-    torch.cuda.synchronize()
-    clock_info = clocks.stop()
-    ms = start.elapsed_time(end) / args.steps
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        props = torch.cuda.get_device_properties(dev)
+        clocks = ClockSampler(f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
+        clocks.start()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            loss = step()
+        end.record()
+        torch.cuda.synchronize()
+        clock_info = clocks.stop()
+    finally:
+        dit.activation_cpu_offload = ours_offload
+    ms = start.elapsed_time(end) / steps
     tokens = args.batch * (img_tokens + txt_tokens)
-    print(json.dumps({
-        "impl": "reference_gpu_modules",
-        "metric": "INT8-W DiT train tokens/s (reference modules on the same GPU)",
-        "value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": args.steps,
-        "warmup": args.warmup, "loss": float(loss.item()), "swapped": swapped,
-        "offload": not args.no_offload, "clocks": clock_info,
+    return {
+        "value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warmup,
+        "loss": float(loss.item()), "swapped": swapped, "offload": not args.no_offload, "clocks": clock_info,
         "note": "training.quantization.FrozenInt8Linear (backend triton), training.lora.LoRALinear and "
                 "training.activation_offload from baseline/_ref in place of this library's modules; "
                 "the rest of the synthetic model, the inputs and AdamW are the default run's",
-    }), flush=True)
+    }
+
+
+def run_train_ref_modules(args: argparse.Namespace) -> None:
+    """One JSON line: `time_reference_modules` at `--steps` after `--warmup`."""
+    result = time_reference_modules(args, args.steps, args.warmup)
+    print(json.dumps({"impl": "reference_gpu_modules",
+                      "metric": "INT8-W DiT train tokens/s (reference modules on the same GPU)", **result}),
+          flush=True)
 
 
 def run_packed(args: argparse.Namespace) -> None:
@@ -1029,6 +1041,17 @@ def run_train(args: argparse.Namespace) -> None:
             line["block_swap"] = block_swap_summary(swap0, swap1, args.steps, elapsed_ms, dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()
+        if world == 1 and not args.no_ref_gpu_arm:
+            # The same step with the reference's own modules on this GPU (after this run's
+            # model is freed); a failure is recorded, not raised.
+            del model, opt, params, reducer
+            torch.cuda.empty_cache()
+            try:
+                ref = time_reference_modules(args, steps=2, warmup=1)
+                line["reference_gpu_modules"] = ref
+                line["speedup_vs_reference_gpu_modules"] = line["value"] / ref["value"]
+            except Exception as error:
+                line["reference_gpu_modules"] = {"unavailable": f"{type(error).__name__}: {error}"[:300]}
         print(json.dumps(line), flush=True)
     qk.set_launch_observer(None)
     if world > 1:
