@@ -65,7 +65,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--offload-pairs", type=int, default=2,
                    help="alternated (offload off, offload on) arm pairs timed after the main region (0: none)")
     p.add_argument("--offload-arm-steps", type=int, default=3)
-    p.add_argument("--offload-defer-mb", type=int, default=640,
+    p.add_argument("--offload-defer-mb", type=int, default=1536,
                    help="keep up to this many MiB of the newest saved activations on the GPU (copied out only when "
                         "newer ones push them past the budget)")
     p.add_argument("--kernel", choices=["gemm_fwd", "gemm_dx", "hadamard", "convrot_fwd", "convrot_dx",
