@@ -649,20 +649,28 @@ def swap_in_reference_modules(model, device) -> dict:
             ref.weight_scale.copy_(mod.weight_scale)
         return ref
 
-    counts = {"int8": 0, "lora": 0}
-    for name, parent in list(model.named_modules()):
-        for child_name, child in list(parent.named_children()):
+    # collect first (a LoRA wrapper's base is replaced together with the wrapper), then swap
+    targets = []
+    for parent in model.modules():
+        if isinstance(parent, OurLoRA):
+            continue
+        for child_name, child in parent.named_children():
             if isinstance(child, OurLoRA) and isinstance(child.base, OurInt8):
-                wrapped = RefLoRA(ref_int8(child.base), child.rank, child.alpha).to(device)
-                with torch.no_grad():
-                    wrapped.lora_A.copy_(child.lora_A)
-                    wrapped.lora_B.copy_(child.lora_B)
-                setattr(parent, child_name, wrapped)
-                counts["lora"] += 1
-                counts["int8"] += 1
+                targets.append((parent, child_name, child, True))
             elif isinstance(child, OurInt8):
-                setattr(parent, child_name, ref_int8(child))
-                counts["int8"] += 1
+                targets.append((parent, child_name, child, False))
+    counts = {"int8": 0, "lora": 0}
+    for parent, child_name, child, is_lora in targets:
+        if is_lora:
+            wrapped = RefLoRA(ref_int8(child.base), child.rank, child.alpha).to(device)
+            with torch.no_grad():
+                wrapped.lora_A.copy_(child.lora_A)
+                wrapped.lora_B.copy_(child.lora_B)
+            setattr(parent, child_name, wrapped)
+            counts["lora"] += 1
+        else:
+            setattr(parent, child_name, ref_int8(child))
+        counts["int8"] += 1
     dit.activation_cpu_offload = ref_ao.activation_cpu_offload
     return counts
 
