@@ -44,13 +44,16 @@ constexpr int kFwdRows = 16;     // output features per forward CTA
 constexpr int kFwdSlab = 64;     // reduction elements per forward slab (16 codes per lane x 4 lanes)
 constexpr int kDxCols = 128;     // output columns per grad-input CTA
 constexpr int kDxSlab = 16;      // reduction rows per grad-input slab
-// Slabs whose weight loads a warp issues before it decodes any of them: 3 x 1 KB (forward) or
-// 2 x 2 KB (grad-input) per warp. The forward's 64-register budget fits four CTAs (32 warps)
-// per SM, ~96 KB of weight loads in flight. Measured on the forward shapes (CUDA-graph timed,
-// 2 x 3072 -> 18432): 3 slabs x 4 CTAs 14.7 us, 4 x 3 16.5 us, 2 x 5 15.9 us, 6 x 2 19.2 us;
-// a per-warp cp.async ring of 4-8 slabs in shared memory instead of registers, 16.5-17.3 us.
+// Weight loads in flight per warp: the forward keeps kFwdBatch slabs of 1 KB in rotating
+// register slots (a slot is refilled as soon as its last word is decoded, so the count never
+// drains between batches); the grad-input issues batches of kDxBatch slabs of 2 KB. The
+// forward's 64-register budget fits four CTAs (32 warps) per SM. Measured on the forward
+// shapes (CUDA-graph timed, 2 x 3072 -> 18432): rotating 2 slots 14.75 us, 3 slots 15.5,
+// 4 slots at 3 CTAs per SM 16.9; batches that drain before the next refill: 3 x 4
+// CTAs 14.7-14.8 us, 4 x 3 16.5, 2 x 5 15.9, 6 x 2 19.2; a per-warp cp.async ring of 4-8 slabs
+// in shared memory 16.5-17.3 us. At 16 rows the rotating slots are 8% faster (21.1 vs 23.0 us).
 #ifndef MOSS_STREAM_FWD_BATCH
-#define MOSS_STREAM_FWD_BATCH 3
+#define MOSS_STREAM_FWD_BATCH 2
 #endif
 #ifndef MOSS_STREAM_CTAS_PER_SM
 #define MOSS_STREAM_CTAS_PER_SM 2
@@ -177,24 +180,25 @@ __global__ void __launch_bounds__(kThreads, kMT == 1 ? kMinCtasPerSm : 2) w8_str
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[mt][i] = 0.0f;
 
-  for (int sl = sl0 + warp; sl < sl1; sl += kWarps * kFwdBatch) {
-    // the weight slices of the whole batch are requested first; the activations (a few KB per
-    // CTA, L1-resident after the first touch) are loaded just before each slab is used
-    uint4 qa[kFwdBatch], qb[kFwdBatch];
+  // Rotating slots: slot u holds the slab kFwdBatch positions ahead of the one being decoded;
+  // it is refilled as soon as its last word is decoded, so every warp keeps kFwdBatch slabs
+  // of weight loads in flight instead of draining to none at the end of each batch.
+  uint4 qa[kFwdBatch], qb[kFwdBatch];
 #pragma unroll
-    for (int u = 0; u < kFwdBatch; ++u) {
-      const int slab = sl + kWarps * u;
-      if (slab < sl1) {
-        const int k0 = slab * kFwdSlab;
-        qa[u] = ldg_stream(wa + k0);
-        qb[u] = ldg_stream(wb + k0);
-      }
+  for (int u = 0; u < kFwdBatch; ++u) {
+    const int slab = sl0 + warp + kWarps * u;
+    if (slab < sl1) {
+      qa[u] = ldg_stream(wa + slab * kFwdSlab);
+      qb[u] = ldg_stream(wb + slab * kFwdSlab);
     }
+  }
+  for (int sl = sl0 + warp; sl < sl1; sl += kWarps * kFwdBatch) {
 #pragma unroll
     for (int u = 0; u < kFwdBatch; ++u) {
       const int slab = sl + kWarps * u;
       if (slab >= sl1) break;
       const int k0 = slab * kFwdSlab;
+      const int next = slab + kWarps * kFwdBatch;
       uint4 xs[kMT][2];
 #pragma unroll
       for (int mt = 0; mt < kMT; ++mt) {
@@ -211,6 +215,10 @@ __global__ void __launch_bounds__(kThreads, kMT == 1 ? kMinCtasPerSm : 2) w8_str
         uint32_t r0, r1, r2, r3;
         da.word(word_of(qa[u], j), a.w_kind, r0, r2);
         db.word(word_of(qb[u], j), a.w_kind, r1, r3);
+        if (j == 3 && next < sl1) {
+          qa[u] = ldg_stream(wa + next * kFwdSlab);
+          qb[u] = ldg_stream(wb + next * kFwdSlab);
+        }
 #pragma unroll
         for (int mt = 0; mt < kMT; ++mt) {
           const uint4& xw = xs[mt][j >> 1];
