@@ -287,43 +287,90 @@ __global__ void __launch_bounds__(kThreads) w8_stream_dx_kernel(const Args a, in
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[mt][j][i] = 0.0f;
 
-  for (int sl = sl0 + warp; sl < sl1; sl += kWarps * kDxBatch) {
+  // With 9-16 rows (two n8 tiles) each slab carries twice the MMA work, and rotating slots
+  // (a slot refilled with the slab two positions ahead as soon as its last word is decoded)
+  // were 10% faster at 16 rows; with up to 8 rows they were 4-9% slower than batches of
+  // kDxBatch slabs that drain before the next refill (CUDA-graph timed, 3072-18432 wide).
+  if constexpr (kMT == 2) {
     uint4 q[kDxBatch][4];
     float sc[kDxBatch][4];
+    auto load_slab = [&](int u, int slab) {
+      const int r0 = slab * kDxSlab + 4 * t;  // this lane's four reduction rows
 #pragma unroll
-    for (int u = 0; u < kDxBatch; ++u) {
-      const int slab = sl + kWarps * u;
-      if (slab < sl1) {
-        const int r0 = slab * kDxSlab + 4 * t;  // this lane's four reduction rows
+      for (int i = 0; i < 4; ++i) {
+        q[u][i] = ldg_stream(wcol + static_cast<int64_t>(r0 + i) * a.ldw);
+        sc[u][i] = __ldg(a.scale + r0 + i);
+      }
+    };
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          q[u][i] = ldg_stream(wcol + static_cast<int64_t>(r0 + i) * a.ldw);
-          sc[u][i] = __ldg(a.scale + r0 + i);
+    for (int u = 0; u < kDxBatch; ++u)
+      if (sl0 + warp + kWarps * u < sl1) load_slab(u, sl0 + warp + kWarps * u);
+    for (int sl = sl0 + warp; sl < sl1; sl += kWarps * kDxBatch) {
+#pragma unroll
+      for (int u = 0; u < kDxBatch; ++u) {
+        const int slab = sl + kWarps * u;
+        if (slab >= sl1) break;
+        const int next = slab + kWarps * kDxBatch;
+        uint2 dy[kMT];
+#pragma unroll
+        for (int mt = 0; mt < kMT; ++mt) dy[mt] = dv[mt] ? ldg8(dyr[mt] + slab * kDxSlab) : make_uint2(0, 0);
+        PairDec<kV, kFast> d01, d23;
+        d01.set(sc[u][0], sc[u][1], a.w_kind);
+        d23.set(sc[u][2], sc[u][3], a.w_kind);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;  // bytes (2j, 2j+1) of two rows, interleaved
+          const uint32_t u01 = prmt(word_of(q[u][0], j >> 1), word_of(q[u][1], j >> 1), sel);
+          const uint32_t u23 = prmt(word_of(q[u][2], j >> 1), word_of(q[u][3], j >> 1), sel);
+          uint32_t r0, r1, r2, r3;
+          d01.word(u01, a.w_kind, r0, r1);
+          d23.word(u23, a.w_kind, r2, r3);
+          if (j == 7 && next < sl1) load_slab(u, next);
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt) mma16816<kV>(acc[mt][j], r0, r1, r2, r3, dy[mt].x, dy[mt].y);
         }
       }
     }
+  } else {
+    for (int sl = sl0 + warp; sl < sl1; sl += kWarps * kDxBatch) {
+      uint4 q[kDxBatch][4];
+      float sc[kDxBatch][4];
 #pragma unroll
-    for (int u = 0; u < kDxBatch; ++u) {
-      const int slab = sl + kWarps * u;
-      if (slab >= sl1) break;
-      uint2 dy[kMT];
+      for (int u = 0; u < kDxBatch; ++u) {
+        const int slab = sl + kWarps * u;
+        if (slab < sl1) {
+          const int r0 = slab * kDxSlab + 4 * t;  // this lane's four reduction rows
 #pragma unroll
-      for (int mt = 0; mt < kMT; ++mt) dy[mt] = dv[mt] ? ldg8(dyr[mt] + slab * kDxSlab) : make_uint2(0, 0);
-      PairDec<kV, kFast> d01, d23;
-      d01.set(sc[u][0], sc[u][1], a.w_kind);
-      d23.set(sc[u][2], sc[u][3], a.w_kind);
+          for (int i = 0; i < 4; ++i) {
+            q[u][i] = ldg_stream(wcol + static_cast<int64_t>(r0 + i) * a.ldw);
+            sc[u][i] = __ldg(a.scale + r0 + i);
+          }
+        }
+      }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;  // bytes (2j, 2j+1) of two rows, interleaved
-        const uint32_t u01 = prmt(word_of(q[u][0], j >> 1), word_of(q[u][1], j >> 1), sel);
-        const uint32_t u23 = prmt(word_of(q[u][2], j >> 1), word_of(q[u][3], j >> 1), sel);
-        uint32_t r0, r1, r2, r3;
-        d01.word(u01, a.w_kind, r0, r1);
-        d23.word(u23, a.w_kind, r2, r3);
+      for (int u = 0; u < kDxBatch; ++u) {
+        const int slab = sl + kWarps * u;
+        if (slab >= sl1) break;
+        uint2 dy[kMT];
 #pragma unroll
-        for (int mt = 0; mt < kMT; ++mt) mma16816<kV>(acc[mt][j], r0, r1, r2, r3, dy[mt].x, dy[mt].y);
+        for (int mt = 0; mt < kMT; ++mt) dy[mt] = dv[mt] ? ldg8(dyr[mt] + slab * kDxSlab) : make_uint2(0, 0);
+        PairDec<kV, kFast> d01, d23;
+        d01.set(sc[u][0], sc[u][1], a.w_kind);
+        d23.set(sc[u][2], sc[u][3], a.w_kind);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t sel = (j & 1) ? 0x7362u : 0x5140u;  // bytes (2j, 2j+1) of two rows, interleaved
+          const uint32_t u01 = prmt(word_of(q[u][0], j >> 1), word_of(q[u][1], j >> 1), sel);
+          const uint32_t u23 = prmt(word_of(q[u][2], j >> 1), word_of(q[u][3], j >> 1), sel);
+          uint32_t r0, r1, r2, r3;
+          d01.word(u01, a.w_kind, r0, r1);
+          d23.word(u23, a.w_kind, r2, r3);
+#pragma unroll
+          for (int mt = 0; mt < kMT; ++mt) mma16816<kV>(acc[mt][j], r0, r1, r2, r3, dy[mt].x, dy[mt].y);
+        }
       }
     }
+
   }
 
   // D fragment of tile j: (column 16 g + 2 j, tokens 2t, 2t+1), (column 16 g + 2 j + 1, same)
