@@ -241,6 +241,39 @@ __device__ __forceinline__ void smem_phase(float* tile, int nrows) {
   __syncthreads();
 }
 
+// The last phase of a tile: as smem_phase, but each thread stores its 16 outputs (already
+// rounded to the storage kind) straight to global memory instead of back to shared memory.
+// For a fixed i the 16 lanes of a half-warp store 16 consecutive elements (32 bytes).
+template <int kKind>
+__device__ __forceinline__ uint16_t storage_bits(float v) {
+  if constexpr (kKind == kBF16) {
+    return static_cast<uint16_t>(__float_as_uint(v) >> 16);
+  } else {
+    return __half_as_ushort(__float2half_rn(v));
+  }
+}
+template <int kKind, int LOG2G, int P>
+__device__ __forceinline__ void smem_phase_store(const float* tile, int nrows, uint16_t* y_tile) {
+  constexpr int kLow = 4 * P;
+  constexpr int kNB = (LOG2G - kLow) < 4 ? (LOG2G - kLow) : 4;
+  constexpr int kHiBits = LOG2G - kLow - kNB;
+  constexpr int kN = 1 << kNB;
+  const int lines = (nrows << LOG2G) >> kNB;
+  for (int line = threadIdx.x; line < lines; line += kThreads) {
+    const int lo = line & ((1 << kLow) - 1);
+    const int rest = line >> kLow;
+    const int hi = rest & ((1 << kHiBits) - 1);
+    const int row = rest >> kHiBits;
+    const int base = (row << LOG2G) + lo + (hi << (kLow + kNB));
+    float w[16];
+#pragma unroll
+    for (int i = 0; i < kN; ++i) w[i] = tile[padded(base + (i << kLow))];
+    phase_stages<kKind, kNB>(w);
+#pragma unroll
+    for (int i = 0; i < kN; ++i) y_tile[base + (i << kLow)] = storage_bits<kKind>(w[i]);
+  }
+}
+
 // The tensor is contiguous [rows, cols] with cols a multiple of the group, so its flat view is
 // a sequence of whole groups: a tile is kFastTile consecutive elements (kFastTile / group
 // groups), and the last tile holds the remaining whole groups. Each thread owns 16 consecutive
@@ -305,14 +338,13 @@ __global__ void __launch_bounds__(kThreads, 5)
         for (int i = 0; i < 16; ++i) tile[padded(e0 + i)] = v[i];
       }
       __syncthreads();
-      smem_phase<kKind, LOG2G, 1>(tile, nrows);
-      if constexpr (kPhases > 2) smem_phase<kKind, LOG2G, 2>(tile, nrows);
-      if (live) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = tile[padded(e0 + i)];
+      if constexpr (kPhases > 2) {
+        smem_phase<kKind, LOG2G, 1>(tile, nrows);
+        smem_phase_store<kKind, LOG2G, 2>(tile, nrows, y + base);
+      } else {
+        smem_phase_store<kKind, LOG2G, 1>(tile, nrows, y + base);
       }
-    }
-    if (live) {
+    } else if (live) {
       uint32_t w[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
