@@ -676,7 +676,7 @@ def swap_in_reference_modules(model, device) -> dict:
 
 
 def time_reference_modules(args: argparse.Namespace, steps: int, warmup: int) -> dict:
-    """The BASELINE config-3 step (same model, inputs, optimizer and offload setting as the
+    """The benchmark's config-3 training step (same model, inputs, optimizer and offload setting as the
     default run) with the reference's own hot-path modules swapped in, timed the same way
     (CUDA events over `steps` after `warmup`, 1 GPU). Returns the measurement."""
     import torch
