@@ -256,15 +256,27 @@ __global__ void __launch_bounds__(kThreads, kMT == 1 ? kMinCtasPerSm : 2) w8_str
 }
 
 // ------------------------------------------------------------------------------- grad-input
-// grid = (Nc / 128) * splits; block = 256; dynamic shared memory = red. CTA b: output strip
-// b / splits (128 columns of dX), reduction split b % splits (slabs of 16 weight rows).
+// grid = (Nc / 128) * splits; block = 256; dynamic shared memory = red. CTA b: one output strip
+// (128 columns of dX) and one reduction split (slabs of 16 weight rows), ordered as below.
 template <int kV, bool kFast, int kMT>
 __global__ void __launch_bounds__(kThreads) w8_stream_dx_kernel(const Args a, int splits, int per_split) {
   constexpr int kRedStride = kDxCols + 1;
   extern __shared__ float red_dyn[];  // [kWarps][8 * kMT][kRedStride]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int strip = blockIdx.x / splits, split = blockIdx.x - strip * splits;
+  // With up to 8 rows consecutive CTAs take the strips of one reduction range, so CTAs resident
+  // together read whole weight rows (every 128-byte strip of them) rather than one strip of many
+  // rows: 1-5% faster at 1-8 rows, 20% slower at 16 rows, which keep split-major order
+  // (CUDA-graph timed, 3072-18432 wide).
+  int strip, split;
+  if constexpr (kMT == 1) {
+    const int strips = a.Nc / kDxCols;
+    split = blockIdx.x / strips;
+    strip = blockIdx.x - split * strips;
+  } else {
+    strip = blockIdx.x / splits;
+    split = blockIdx.x - strip * splits;
+  }
   const int k0 = strip * kDxCols;  // first output column of the strip
   const int slabs = a.w_rows / kDxSlab;
   const int sl0 = split * per_split, sl1 = min(slabs, sl0 + per_split);
